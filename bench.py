@@ -1,0 +1,589 @@
+#!/usr/bin/env python
+"""Decode state-op benchmark of the tiered Mamba2 state update (nested_ssm "v4").
+
+Metric: decode state-op tokens/s at B=448 over 27 Mamba2 layers,
+Nemotron-Nano-9B-v2 shapes (H=128, P=80, N=128, G=8), hot 32 dims fp32, cold 96
+dims fp8 e4m3 with one fp32 scale per (seq, head, headdim row), c=4.  One step =
+one decode token through all 27 layers' state ops (rotation of B and C by R, the
+tiered update with its ring write and rank-c flush).  Synthetic seeded inputs with
+the BASELINE distributions; the state pool (29 GB) is far larger than L2, so no
+L2 flush is needed between steps.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 runs under torchrun: every rank owns its own slot pool and batch of 448
+(weak scaling, no data-path collective).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+import torch  # noqa: E402
+
+H, P, N, G = 128, 80, 128, 8
+METRIC = "decode state-op tokens/s at B=448 (27 layers)"
+# Published reference number for this exact configuration: tiered fp8-cold c=4 at
+# B=448 ran at 0.68x the fla fresh op of 51.45 ms/step (8,707 tok/s): 5,921 tok/s.
+REF_PUBLISHED_TOKS = 0.68 * 8707.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=448)
+    ap.add_argument("--layers", type=int, default=27)
+    ap.add_argument("--chunk", type=int, default=4)
+    ap.add_argument("--hot", type=int, default=32)
+    ap.add_argument("--cold", choices=["fp8", "bf16", "fp32"], default="fp8")
+    ap.add_argument("--no-fresh", action="store_true", help="skip the untiered fresh control")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--cpu-sample-batch", type=int, default=4)
+    ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of replaying CUDA graphs")
+    return ap.parse_args()
+
+
+# --------------------------------------------------------------------------
+# algorithmic bytes (per token, per layer, per sequence) of the tiered step kernel
+# --------------------------------------------------------------------------
+def step_bytes_per_seq(c: int, pb: int, cold: str, io_bytes: int = 2, out_bytes: int = 2) -> float:
+    """Algorithmic HBM bytes of one tiered state update (STEP + FLUSH launches) for one
+    sequence-token-layer, averaged over a c-token cycle.
+
+    STEP: hot read+write, cold (+ row scales) read, x / dt / rotated B, C in, y out,
+    glog and t read+write, this token's ring entry written.  FLUSH (once per c tokens):
+    cold (+ scales) read and written, the c ring entries read."""
+    s = {"fp8": 1, "bf16": 2, "fp32": 4}[cold]
+    Nc = N - pb
+    scale = H * P * 4 if cold == "fp8" else 0
+    ring_w = H * P * io_bytes + H * 4 + G * Nc * io_bytes
+    step = (2 * H * P * pb * 4 + H * P * Nc * s + scale + H * P * io_bytes + H * 2
+            + 2 * G * N * io_bytes + H * P * out_bytes + 2 * H * 4 + 2 * H * 4 + ring_w)
+    flush = 2 * (H * P * Nc * s + scale) + c * ring_w
+    return step + flush / c
+
+
+def survey_bytes_per_seq(c: int) -> float:
+    """Byte model the reference's design implies (separate flush, fp32 ring)."""
+    return 3_780_872 + 2_048_000 / c
+
+
+def fresh_bytes_per_seq(io_bytes=2, out_bytes=2) -> float:
+    return 2 * H * P * N * 4 + H * P * io_bytes + H * 2 + 2 * G * N * io_bytes + H * P * out_bytes
+
+
+def load_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def load_traffic():
+    """Per-launch DRAM bytes of the step kernel from the committed ncu summary."""
+    path = os.path.join(REPO, "profiles", "ncu_traffic.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f)
+    return None
+
+
+# --------------------------------------------------------------------------
+# clocks sampled during the timed region
+# --------------------------------------------------------------------------
+class ClockSampler:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        # nvidia-smi numbers GPUs physically; address ours by UUID
+        self.idx = str(gpu_index)
+        try:
+            u = str(torch.cuda.get_device_properties(gpu_index).uuid)
+            self.idx = u if u.startswith("GPU-") else "GPU-" + u
+        except Exception:
+            pass
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", self.idx], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for nm, v in zip(names, r[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]), "samples": len(rows),
+                "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit()) if rows else None,
+                "reasons": sorted(reasons)}
+
+
+# --------------------------------------------------------------------------
+# distributed plumbing
+# --------------------------------------------------------------------------
+def dist_init():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    return rank, ws, local
+
+
+def barrier(ws):
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(v: float, ws: int) -> float:
+    if ws == 1:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# --------------------------------------------------------------------------
+# workload
+# --------------------------------------------------------------------------
+class Workload:
+    """L layers of state ops for B sequences on this rank, inputs resident in HBM."""
+
+    NI = 4  # distinct per-step input sets cycled through
+
+    def __init__(self, args, rank: int):
+        from nested_ssm_b200 import TieredSlotPool, prefill_split
+        self.args = args
+        dev = torch.device("cuda")
+        L, B = args.layers, args.batch
+        self.L, self.B = L, B
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(1000 + rank)
+        self.pool = TieredSlotPool(L, B, H, P, N, G, args.hot, args.chunk, args.cold, torch.bfloat16, dev,
+                                   max_batch=B)
+        slots = torch.arange(B, dtype=torch.int32, device=dev)
+        self.slots = slots
+        # per-layer parameters with the BASELINE distributions
+        self.A, self.D, self.dtb, self.R = [], [], [], []
+        for l in range(L):
+            self.A.append(-torch.exp(torch.rand(H, device=dev, generator=gen) * math.log(16.0)))
+            self.D.append(torch.randn(H, device=dev, generator=gen))
+            u = torch.rand(H, device=dev, generator=gen) * (0.1 - 1e-3) + 1e-3
+            self.dtb.append(torch.log(torch.expm1(u)))
+            self.R.append(torch.linalg.qr(torch.randn(G, N, N, device=dev, generator=gen))[0].contiguous())
+            # prefill: initial state ~ N(0, 0.1), split into hot fp32 / cold fp8
+            st = torch.randn(B, H, P, N, device=dev, generator=gen) * math.sqrt(0.1)
+            prefill_split(self.pool, l, st, slots)
+            del st
+        NI = self.NI
+        self.x = torch.randn(NI, L, B, H, P, device=dev, generator=gen).to(torch.bfloat16)
+        self.dt = torch.randn(NI, L, B, H, device=dev, generator=gen).to(torch.bfloat16)
+        self.BC = (torch.randn(NI, L, 2 * B, G * N, device=dev, generator=gen) / math.sqrt(N)).to(torch.bfloat16)
+        self.BCr = torch.empty(2 * B, G * N, dtype=torch.bfloat16, device=dev)
+        self.y = torch.empty(L, B, H, P, dtype=torch.bfloat16, device=dev)
+        torch.cuda.synchronize()
+
+    def layer(self, l: int, k: int, ev=None):
+        """One layer's state op for input set k: rotation (one launch for B and C) then
+        the tiered step kernel."""
+        from nested_ssm_b200 import rot_flat, tiered_state_update
+        i = k % self.NI
+        B = self.B
+        if ev is not None:
+            ev[0].record()
+        rot_flat(self.BC[i, l], self.R[l], out=self.BCr)
+        if ev is not None:
+            ev[1].record()
+        tiered_state_update(self.pool, l, self.x[i, l], self.dt[i, l], self.A[l], self.BCr[:B].view(B, G, N),
+                            self.BCr[B:].view(B, G, N), self.D[l], self.dtb[l], True, self.slots, -1, self.y[l],
+                            None, 1e-3)
+        if ev is not None:
+            ev[2].record()
+
+    def step(self, k: int, evs=None):
+        for l in range(self.L):
+            self.layer(l, k, None if evs is None else evs[l])
+
+
+def time_fresh(args, rank: int, ws: int):
+    """Untiered fp32 fresh update (own kernel) on the same shapes: tokens/s."""
+    from nested_ssm_b200 import rot_flat, selective_state_update
+    dev = torch.device("cuda")
+    L, B = args.layers, args.batch
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(2000 + rank)
+    state = torch.empty(L, B, H, P, N, device=dev)
+    for l in range(L):
+        state[l].normal_(0.0, math.sqrt(0.1), generator=gen)
+    A = -torch.exp(torch.rand(L, H, device=dev, generator=gen) * math.log(16.0))
+    D = torch.randn(L, H, device=dev, generator=gen)
+    dtb = torch.log(torch.expm1(torch.rand(L, H, device=dev, generator=gen) * (0.1 - 1e-3) + 1e-3))
+    R = [torch.linalg.qr(torch.randn(G, N, N, device=dev, generator=gen))[0].contiguous() for _ in range(L)]
+    x = torch.randn(L, B, H, P, device=dev, generator=gen).to(torch.bfloat16)
+    dt = torch.randn(L, B, H, device=dev, generator=gen).to(torch.bfloat16)
+    BC = (torch.randn(L, 2 * B, G * N, device=dev, generator=gen) / math.sqrt(N)).to(torch.bfloat16)
+    BCr = torch.empty(2 * B, G * N, dtype=torch.bfloat16, device=dev)
+    y = torch.empty(L, B, H, P, dtype=torch.bfloat16, device=dev)
+    slots = torch.arange(B, dtype=torch.int32, device=dev)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(L)]
+    kdur = []
+
+    def step(timed=False):
+        for l in range(L):
+            if timed:
+                evs[l][0].record()
+            rot_flat(BC[l], R[l], out=BCr)
+            if timed:
+                evs[l][1].record()
+            selective_state_update(state[l], x[l], dt[l], A[l], BCr[:B].view(B, G, N), BCr[B:].view(B, G, N),
+                                   D[l], None, dtb[l], True, slots, -1, y[l])
+            if timed:
+                evs[l][2].record()
+
+    K = max(4, args.steps // 4)
+    for _ in range(max(3, args.warmup // 2)):
+        step()
+    barrier(ws)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(K):
+        step(timed=True)
+        torch.cuda.synchronize()
+        kdur += [evs[l][1].elapsed_time(evs[l][2]) for l in range(L)]
+    e1.record()
+    torch.cuda.synchronize()
+    # the per-step syncs above add host gaps: time once more without them
+    e0.record()
+    for _ in range(K):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / K, ws)
+    barrier(ws)
+    del state, x, BC, y
+    torch.cuda.empty_cache()
+    kms = statistics.mean(kdur)
+    return {"tokens_per_s": ws * B / (ms / 1e3), "ms_per_step": ms,
+            "kernel_ms": kms, "kernel_gbs": B * fresh_bytes_per_seq() / (kms / 1e3) / 1e9}
+
+
+def time_e2e(wl: Workload, args, ws: int):
+    """Same metric through the public API with HOST buffers: every step copies that
+    step's inputs (x, dt, B, C of all layers) from pinned host memory and reads y
+    back; copies overlap compute on separate streams, layer by layer."""
+    from nested_ssm_b200 import rot_flat, tiered_state_update
+    L, B = wl.L, wl.B
+    dev = torch.device("cuda")
+    hx = wl.x[0].cpu().pin_memory()
+    hdt = wl.dt[0].cpu().pin_memory()
+    hBC = wl.BC[0].cpu().pin_memory()
+    hy = torch.empty(L, B, H, P, dtype=torch.bfloat16).pin_memory()
+    dx = torch.empty_like(wl.x[0])
+    ddt = torch.empty_like(wl.dt[0])
+    dBC = torch.empty_like(wl.BC[0])
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+    comp = torch.cuda.current_stream()
+    ev_in = [torch.cuda.Event() for _ in range(L)]
+    ev_done = [torch.cuda.Event() for _ in range(L)]
+    first = [True]
+    h2d = (hx.numel() * hx.element_size() + hdt.numel() * hdt.element_size() + hBC.numel() * hBC.element_size())
+    d2h = hy.numel() * hy.element_size()
+
+    def step():
+        for l in range(L):
+            with torch.cuda.stream(s_in):
+                if not first[0]:
+                    s_in.wait_event(ev_done[l])        # previous step consumed buffer l
+                dx[l].copy_(hx[l], non_blocking=True)
+                ddt[l].copy_(hdt[l], non_blocking=True)
+                dBC[l].copy_(hBC[l], non_blocking=True)
+                ev_in[l].record(s_in)
+            comp.wait_event(ev_in[l])
+            rot_flat(dBC[l], wl.R[l], out=wl.BCr)
+            tiered_state_update(wl.pool, l, dx[l], ddt[l], wl.A[l], wl.BCr[:B].view(B, G, N),
+                                wl.BCr[B:].view(B, G, N), wl.D[l], wl.dtb[l], True, wl.slots, -1, wl.y[l],
+                                None, 1e-3)
+            ev_done[l].record(comp)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(ev_done[l])
+                hy[l].copy_(wl.y[l], non_blocking=True)
+        first[0] = False
+
+    K = max(4, args.steps // 2)
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    barrier(ws)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(K):
+        step()
+    comp.wait_stream(s_out)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / K, ws)
+    barrier(ws)
+    return {"value": round(ws * B / (ms / 1e3), 1), "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(d2h), "ms_per_step": round(ms, 3),
+            "wall_ms_per_step": round((time.perf_counter() - t0) * 1e3 / K, 3)}
+
+
+# --------------------------------------------------------------------------
+# CPU legs (the oracle port -- the reference's own path is Python/torch)
+# --------------------------------------------------------------------------
+def cpu_sample(args, batch: int, steps: int, warmup: int, threads: int):
+    """Time the CPU oracle (tiered replay semantics, torch eager) on `batch` sequences
+    x all layers; returns tokens/s and a description."""
+    import oracle as O
+    torch.set_num_threads(threads)
+    L = args.layers
+    cold = {"fp8": O.FP8, "bf16": torch.bfloat16, "fp32": torch.float32}[args.cold]
+    prms = O.make_params(H, G, N, seed=0, layers=L)
+    pools = []
+    for l in range(L):
+        pool = O.TieredPoolRef(batch, H, P, N, G, args.hot, args.chunk, cold, torch.bfloat16)
+        O.prefill_split(pool, torch.arange(batch), torch.randn(batch, H, P, N) * math.sqrt(0.1))
+        pools.append(pool)
+    xs, dts, Bs, Cs = O.make_inputs(batch, H, P, G, N, args.chunk, seed=0)
+    slots = torch.arange(batch)
+
+    def step(k):
+        i = k % args.chunk
+        for l in range(L):
+            prm = prms[l]
+            Br = O.rot_flat(Bs[i].reshape(batch, -1), prm["R"]).reshape(batch, G, N)
+            Cr = O.rot_flat(Cs[i].reshape(batch, -1), prm["R"]).reshape(batch, G, N)
+            O.tiered_step(pools[l], slots, xs[i], dts[i], Br, Cr, prm["A"], prm["D"], prm["dt_bias"], 1e-3)
+
+    for k in range(warmup):
+        step(k)
+    t0 = time.perf_counter()
+    times = []
+    for k in range(steps):
+        s0 = time.perf_counter()
+        step(k)
+        times.append(time.perf_counter() - s0)
+    el = time.perf_counter() - t0
+    return {"tokens_per_s": batch * steps / el, "step_s": times}
+
+
+def cpu_baseline_leg(args):
+    threads = os.cpu_count() or 1
+    r = cpu_sample(args, args.cpu_sample_batch, args.chunk, 1, threads)
+    return {"value": round(r["tokens_per_s"], 3), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"oracle (torch eager, {threads} threads): B={args.cpu_sample_batch} sequences x "
+                      f"{args.layers} layers x {args.chunk} steps (one flush cycle), same shapes/dtypes"}
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU path (the oracle port; the reference is
+    Python with no compiled CPU code) on the host cores, rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    batch = args.cpu_sample_batch
+    r = cpu_sample(args, batch, max(1, args.steps), max(0, min(args.warmup, 1)), threads)
+    v = round(r["tokens_per_s"], 3)
+    ms = statistics.mean(r["step_s"]) * 1e3
+    line = {"metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": args.cold + "-cold/fp32-hot", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": f"tiered c={args.chunk} {args.cold}-cold hot={args.hot}, {args.layers} layers, "
+                                   f"sampled at B={batch} (CPU)", "batch": batch, "layers": args.layers},
+            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
+                             "sample": f"B={batch} sequences x {args.layers} layers per step, torch eager CPU"},
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# --------------------------------------------------------------------------
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    rank, ws, local = dist_init()
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device")
+    import nested_ssm_b200  # noqa: F401  (fails loudly if the library is missing)
+    wl = Workload(args, rank)
+    L, B, K, W = wl.L, wl.B, args.steps, max(3, args.warmup)
+
+    # One CUDA graph holds Workload.NI consecutive steps (every layer: rotation then
+    # the tiered update, bracketed by event-record nodes); the flush decision is taken
+    # on the device from the slots' token counts, so replays stay exact.
+    NI = Workload.NI
+    evs = [[[torch.cuda.Event(enable_timing=True, external=True) for _ in range(3)] for _ in range(L)]
+           for _ in range(NI)]
+    for k in range(W):
+        wl.step(k)
+    torch.cuda.synchronize()
+    graph = None
+    if not args.no_graph:
+        cap = torch.cuda.Stream()
+        cap.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(cap):
+            with torch.cuda.graph(graph, stream=cap):
+                for k in range(NI):
+                    wl.step(W + k, evs[k])
+        torch.cuda.current_stream().wait_stream(cap)
+        torch.cuda.synchronize()
+        # (capture did not execute the kernels)
+    reps = max(1, (K + NI - 1) // NI)
+    K = reps * NI
+
+    def run_cycle(k0):
+        if graph is not None:
+            graph.replay()
+        else:
+            for k in range(NI):
+                wl.step(k0 + k, evs[k])
+
+    run_cycle(0)   # warm the graph
+    barrier(ws)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for r in range(reps):
+        run_cycle(r * NI)
+    e1.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = max_over_ranks(e0.elapsed_time(e1) / K, ws)
+    barrier(ws)
+
+    # kernel durations over whole c-cycles (flush and non-flush launches), from the
+    # event-record nodes of further replays
+    kd_all, rd_all = [], []
+    for r in range(max(1, (args.chunk + NI - 1) // NI)):
+        run_cycle(0)
+        torch.cuda.synchronize()
+        for k in range(NI):
+            kd_all += [evs[k][l][1].elapsed_time(evs[k][l][2]) for l in range(L)]
+            rd_all += [evs[k][l][0].elapsed_time(evs[k][l][1]) for l in range(L)]
+    value = ws * B / (ms / 1e3)
+
+    peak, peak_kind = load_peaks()
+    bps = step_bytes_per_seq(args.chunk, args.hot, args.cold)
+    kms = statistics.mean(kd_all) if kd_all else None
+    roof = None
+    if kms:
+        achieved = B * bps / (kms / 1e3) / 1e9
+        tr = load_traffic()
+        traffic = None
+        if tr and tr.get("workload") == f"B{B}_c{args.chunk}_{args.cold}_pb{args.hot}":
+            traffic = tr.get("bytes_per_launch")
+        roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
+                "kernel": "tiered state update (STEP + FLUSH persistent kernels)", "kernel_ms_avg": round(kms, 4),
+                "bytes_per_launch": int(B * bps), "survey_bytes_per_launch": int(B * survey_bytes_per_seq(args.chunk)),
+                "rotation_ms_avg": round(statistics.mean(rd_all), 4) if rd_all else None,
+                "kernel_ms_by_step": [round(statistics.mean(kd_all[i * L:(i + 1) * L]), 4)
+                                      for i in range(len(kd_all) // L)],
+                "step_gbs_incl_rotation": round(L * B * bps / (ms / 1e3) / 1e9, 1)}
+
+    e2e = None if args.no_e2e else time_e2e(wl, args, ws)
+    del wl
+    torch.cuda.empty_cache()
+    fresh = None if args.no_fresh else time_fresh(args, rank, ws)
+
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu:
+        cpu = cpu_baseline_leg(args)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": ws, "steps": K,
+            "warmup": W, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": round(value / (ws * REF_PUBLISHED_TOKS), 3),
+            "dtype": f"{args.cold}-cold/fp32-hot (bf16 io)", "data": "synthetic",
+            "config": {"workload": f"tiered c={args.chunk} {args.cold}-cold hot={args.hot}, B={B}/GPU, "
+                                   f"{L} layers, H={H} P={P} N={N} G={G}",
+                       "batch_per_gpu": B, "layers": L, "chunk": args.chunk, "hot": args.hot, "cold": args.cold,
+                       "parallelism": f"slot-sharded x{ws} (no collective)",
+                       "l2": "inputs larger than L2 (tiered pool %.1f GB/GPU)" % (L * B * bytes_per_slot(args) / 1e9),
+                       "cuda_graph": not args.no_graph},
+            "gpu_launches": K * L * 2,
+            "roofline": roof,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+            "fresh_control": fresh,
+            "speedup_vs_fresh": round(value / fresh["tokens_per_s"], 3) if fresh else None,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
+def bytes_per_slot(args) -> float:
+    s = {"fp8": 1, "bf16": 2, "fp32": 4}[args.cold]
+    Nc = N - args.hot
+    return (H * P * args.hot * 4 + H * P * Nc * s + (H * P * 4 if args.cold == "fp8" else 0) + 2 * H * 4
+            + args.chunk * (H * P * 2 + H * 4 + G * Nc * 2))
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,186 @@
+/*
+ * nested_ssm.h -- C ABI of the B200 tiered Mamba2 decode state op.
+ *
+ * The op keeps each head's SSM state S[P][N] split along N: the first pb
+ * columns ("hot") are fp32 and updated every token; the remaining N-pb
+ * columns ("cold") are stored in fp8 e4m3 (one fp32 scale per headdim row),
+ * bf16 or fp32, read stale with an exp(sum dt*A) decay correction, and folded
+ * forward every c tokens by a rank-c replay of a per-slot ring of the chunk's
+ * (x, dt, B) followed by requantisation.  Slots are addressed through a
+ * continuous-batching index (state_batch_indices); rows whose slot equals
+ * pad_slot_id are skipped on the GPU.
+ *
+ * Conventions
+ *  - Every pointer is a DEVICE pointer owned by the caller; entry points never
+ *    allocate and never synchronise the stream.  `stream` is a cudaStream_t
+ *    (NULL = legacy default stream).
+ *  - Return value: 0 (NSSM_OK) or an nssm_status; nssm_last_error() gives a
+ *    message for the calling thread.  Errors found on the device (a slot
+ *    index outside [0, num_slots)) are OR-ed into *status when status != NULL
+ *    (bit 0: bad slot) and the row is skipped.
+ *  - Strides are in elements.  The innermost dimension of every tensor is
+ *    contiguous.
+ *
+ * Reference interfaces replaced (paths inside omin-Kwon/nested_ssm, plus the
+ * third-party call the reference drives):
+ *  - nssm_tiered_step  : the tiered decode of one layer = vLLM
+ *        selective_state_update (vllm/model_executor/layers/mamba/ops/mamba_ssm.py:493,
+ *        called at mamba_mixer2.py:1030-1046) followed by decode_readout
+ *        (scale/vllm_v4_patch.py:140-179); equivalently the state-op part of
+ *        _v4_fused_decode (scale/v4_fused_decode.py:45-93) and of
+ *        _v4_decode (scale/v4_native_decode.py:49-169).
+ *  - nssm_fresh_step   : untiered selective_state_update (the fresh control,
+ *        scale/bench_v4_decode.py:241-254).
+ *  - nssm_prefill_split: prefill_snapshot (scale/vllm_v4_patch.py:123-137) and the
+ *        prefill capture of scale/v4_fused_decode.py:121-159.
+ *  - nssm_rot_flat     : rot_flat (scale/vllm_v4_patch.py:41-45) / the fp32
+ *        rotation of scale/v4_fused_decode.py:45-48.
+ *  - nssm_materialize  : no single reference function; returns the exact full
+ *        state the native path keeps in cache (scale/v4_native_decode.py:65-67).
+ */
+#ifndef NESTED_SSM_H_
+#define NESTED_SSM_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NSSM_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define NSSM_API __attribute__((visibility("default")))
+#else
+#define NSSM_API
+#endif
+
+typedef enum {
+  NSSM_OK = 0,
+  NSSM_ERR_INVALID = 1,     /* bad argument (shape, pointer, alignment, dtype) */
+  NSSM_ERR_UNSUPPORTED = 2, /* valid but not compiled (e.g. hot width)        */
+  NSSM_ERR_CUDA = 3         /* a CUDA runtime call failed                     */
+} nssm_status;
+
+typedef enum {
+  NSSM_F32 = 0,
+  NSSM_BF16 = 1,
+  NSSM_F8E4M3 = 2
+} nssm_dtype;
+
+typedef enum {
+  NSSM_MODE_STALE = 0,   /* y_cold = exp(glog) C.cold, glog lags one token (default) */
+  NSSM_MODE_CORR = 1,    /* exact rank-c correction (scale/v4_native_decode.py:81-117) */
+  NSSM_MODE_COLDOFF = 2  /* hot-only readout, cold still maintained (draft)          */
+} nssm_mode;
+
+/* One layer's tiered slot pool.  Layouts (row-major, innermost last):
+ *   hot        f32        [num_slots][nheads][headdim][hot_dim]
+ *   cold       cold_dtype [num_slots][nheads][headdim][dstate-hot_dim]
+ *   cold_scale f32        [num_slots][nheads][headdim]   (fp8 only, else NULL)
+ *   glog       f32        [num_slots][nheads]     sum of dt*A since the last flush
+ *   t          i32        [num_slots][nheads]     decode tokens since prefill
+ *   ring_x     io_dtype   [num_slots][nheads][chunk][headdim]
+ *   ring_dt    f32        [num_slots][nheads][round_up(chunk, 4)]
+ *   ring_b     f32        [num_slots][ngroups][chunk][dstate-hot_dim]
+ * All base pointers must be 16-byte aligned. */
+typedef struct {
+  int32_t num_slots, nheads, headdim, dstate, ngroups, hot_dim, chunk;
+  int32_t cold_dtype; /* nssm_dtype */
+  int32_t io_dtype;   /* nssm_dtype of x / B / C / ring (F32 or BF16) */
+  int32_t _pad0;
+  float* hot;
+  void* cold;
+  float* cold_scale;
+  float* glog;
+  int32_t* t;
+  void* ring_x;
+  float* ring_dt;
+  float* ring_b;
+} nssm_pool;
+
+/* Per-token inputs of one layer, in the argument order of
+ * selective_state_update(state, x, dt, A, B, C, D, z, dt_bias, dt_softplus,
+ * state_batch_indices, pad_slot_id, out). */
+typedef struct {
+  int32_t batch;          /* rows in this call                                   */
+  int32_t io_dtype;       /* dtype of x, B, C (F32 or BF16)                     */
+  const void* x;          /* [batch][nheads][headdim]                           */
+  int64_t x_stride_b, x_stride_h;
+  const void* dt;         /* [batch][nheads], pre-softplus                      */
+  int64_t dt_stride_b, dt_stride_h;
+  int32_t dt_dtype;       /* F32 or BF16                                        */
+  int32_t dt_softplus;    /* 1: dt = softplus(dt + dt_bias)                     */
+  const float* A;         /* [nheads] (negative)                               */
+  const void* B;          /* [batch][ngroups][dstate]  (rotated unless R given) */
+  int64_t B_stride_b;
+  const void* C;          /* [batch][ngroups][dstate]                           */
+  int64_t C_stride_b;
+  const float* D;         /* [nheads] or NULL                                   */
+  const float* dt_bias;   /* [nheads] or NULL                                   */
+  float dt_min;           /* dt = max(dt, dt_min) after softplus (<=0: none)    */
+  int32_t mode;           /* nssm_mode                                          */
+  const float* R;         /* [ngroups][dstate][dstate] or NULL: rotate B and C first */
+  const int32_t* state_batch_indices; /* [batch] slot of each row; NULL = row */
+  int32_t pad_slot_id;    /* rows with this slot are skipped                    */
+  int32_t out_dtype;      /* F32 or BF16                                        */
+  void* out;              /* [batch][nheads][headdim]                           */
+  int64_t out_stride_b, out_stride_h;
+  void* workspace;        /* >= nssm_step_workspace_bytes() when R != NULL      */
+  size_t workspace_bytes;
+  int32_t* status;        /* optional device word, error bits OR-ed in          */
+} nssm_step_args;
+
+/* Bytes of workspace nssm_tiered_step / nssm_fresh_step need for `batch` rows
+ * when R != NULL (the rotated B and C), 0 otherwise. */
+NSSM_API size_t nssm_step_workspace_bytes(int32_t batch, int32_t ngroups, int32_t dstate,
+                                 int32_t io_dtype, int32_t has_rotation);
+
+/* Tiered decode of one token for one layer (replaces selective_state_update +
+ * decode_readout, see the header comment).  Updates the pool in place and
+ * writes y = C_hot.h_hot + exp(glog) C_cold.cold + D x to out. */
+NSSM_API int nssm_tiered_step(const nssm_pool* pool, const nssm_step_args* args, void* stream);
+
+/* Untiered fp32 update of a full state [num_slots][nheads][headdim][dstate]
+ * (replaces selective_state_update; the fresh control). */
+NSSM_API int nssm_fresh_step(float* state, int32_t num_slots, int32_t nheads, int32_t headdim,
+                    int32_t dstate, int32_t ngroups, const nssm_step_args* args,
+                    void* stream);
+
+/* Split full fp32 states (row i at state + i*state_stride_b, layout
+ * [nheads][headdim][dstate]) into pool slots[i]: hot <- [:hot_dim],
+ * cold <- quantise([hot_dim:]), glog <- 0, t <- 0.  Replaces prefill_snapshot. */
+NSSM_API int nssm_prefill_split(const nssm_pool* pool, const float* state, int64_t state_stride_b,
+                       const int32_t* slots, int32_t batch, int32_t pad_slot_id,
+                       void* stream);
+
+/* Write the exact current full fp32 state of slots[i] to out + i*out_stride_b
+ * ([nheads][headdim][dstate]): hot, and cold replayed through the ring entries
+ * since the last flush.  Read-only on the pool. */
+NSSM_API int nssm_materialize(const nssm_pool* pool, const float* A, const int32_t* slots,
+                     int32_t batch, int32_t pad_slot_id, float* out, int64_t out_stride_b,
+                     void* stream);
+
+/* out[t][g][m] = sum_n R[g][m][n] x[t][g][n] with fp32 accumulation, rounded
+ * to `dtype` (F32 or BF16).  Replaces rot_flat. */
+NSSM_API int nssm_rot_flat(const void* x, int64_t x_stride, int32_t dtype, const float* R,
+                  int32_t T, int32_t ngroups, int32_t dstate, void* out,
+                  int64_t out_stride, void* stream);
+
+/* Hot widths compiled into this library for a given dstate, written to
+ * widths[0..n) (n <= cap); returns n. */
+NSSM_API int32_t nssm_supported_hot_dims(int32_t dstate, int32_t* widths, int32_t cap);
+
+/* sizeof of the argument structs, for binding checks. */
+NSSM_API size_t nssm_sizeof_pool(void);
+NSSM_API size_t nssm_sizeof_step_args(void);
+
+NSSM_API int32_t nssm_abi_version(void);
+NSSM_API const char* nssm_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NESTED_SSM_H_ */

@@ -1,0 +1,446 @@
+// extern "C" entry points of libnested_ssm: argument validation, dispatch to
+// the compiled (dstate, hot width, cold dtype) instances, and launches on the
+// caller's stream.  Nothing here allocates device memory or synchronises.
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "nssm_persistent.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_check(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(NSSM_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return NSSM_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int io_bytes(int dt) { return dt == NSSM_BF16 ? 2 : 4; }
+
+int round_up(int v, int m) { return (v + m - 1) / m * m; }
+
+using nssm::COLD_BF16;
+using nssm::COLD_F32;
+using nssm::COLD_FP8;
+using nssm::COLD_NONE;
+
+constexpr int kTPR = 2;        // threads per headdim row, tiered kernels
+constexpr int kTPRFresh = 4;   // threads per headdim row, untiered kernel
+
+template <int PB, int NC, int COLD>
+size_t step_smem_bytes(int P, int c) {
+  return sizeof(float) * nssm::StepShape<PB, NC, COLD>::smem_floats(P, c);
+}
+
+// ---- launchers ------------------------------------------------------------
+template <int PB, int NC, int COLD, int TPR>
+int launch_step(const nssm::StepParams& sp, int batch, cudaStream_t st) {
+  dim3 grid(sp.H, batch);
+  const int threads = round_up(sp.P * TPR, 32);
+  nssm::tiered_step_kernel<PB, NC, COLD, TPR><<<grid, threads, step_smem_bytes<PB, NC, COLD>(sp.P, sp.c), st>>>(sp);
+  return cuda_check("tiered_step_kernel launch");
+}
+
+// Per-(kernel, smem size, device) cache of resident CTAs per SM.
+struct OccEntry { const void* fn; int smem; int dev; int occ; };
+OccEntry g_occ[64];
+std::atomic<int> g_nocc{0};
+
+int occupancy(const void* fn, int smem, int threads, int* occ_out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return cuda_check("cudaGetDevice");
+  const int n = g_nocc.load(std::memory_order_acquire);
+  for (int i = 0; i < n && i < 64; ++i)
+    if (g_occ[i].fn == fn && g_occ[i].smem == smem && g_occ[i].dev == dev) {
+      *occ_out = g_occ[i].occ;
+      return NSSM_OK;
+    }
+  // The attribute is one value per function: always opt in to the device maximum so
+  // a later launch with a larger layout (another c / batch) stays legal.
+  int optin = 0;
+  if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
+    return cuda_check("cudaDeviceGetAttribute(smem opt-in)");
+  if (smem > optin) {
+    *occ_out = 0;
+    return NSSM_OK;
+  }
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, optin) != cudaSuccess)
+    return cuda_check("cudaFuncSetAttribute(persistent kernel)");
+  int occ = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, threads, smem) != cudaSuccess)
+    return cuda_check("cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+  const int slot = g_nocc.fetch_add(1, std::memory_order_acq_rel);
+  if (slot < 64) g_occ[slot] = OccEntry{fn, smem, dev, occ};
+  *occ_out = occ;
+  return NSSM_OK;
+}
+
+int sm_count(int* out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return cuda_check("cudaGetDevice");
+  if (cudaDeviceGetAttribute(out, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return cuda_check("cudaDeviceGetAttribute(SM count)");
+  return NSSM_OK;
+}
+
+// The persistent TMA-pipelined kernels move every per-item operand with 1-D bulk
+// copies, so they need 16-byte aligned rows: headdim % 4 == 0 and <= 80, x / B / C
+// bases and strides 16-byte aligned.  Anything else runs the simple kernel.
+template <int PB, int NC, int COLD, bool IOBF, int PHASE, int CFIX>
+int launch_phase(const nssm::StepParams& sp, int batch, cudaStream_t st, bool ring_ok, int sms, bool* done) {
+  *done = false;
+  const long long items = (long long)batch * sp.H;
+  auto fn = nssm::tiered_persistent_kernel<PB, NC, COLD, IOBF, PHASE, CFIX>;
+  const int iob = IOBF ? 2 : 4;
+  const int minb = PHASE == nssm::PH_STEP ? NSSM_STEP_P_MINB : NSSM_FLUSH_P_MINB;
+  for (int target = minb; target >= 1; --target) {
+    long long grid = (long long)sms * target;
+    if (grid > items) grid = items;
+    const long long per_cta = (items + grid - 1) / grid;
+    const int maxb = (int)((per_cta + sp.H - 1) / sp.H) + 2;
+    nssm::PParams pp{};
+    pp.sp = sp;
+    pp.L = nssm::make_playout<PB, NC, COLD>(PHASE, sp.mode == NSSM_MODE_CORR, sp.P, sp.H, sp.c, iob, maxb,
+                                            (int)per_cta, ring_ok);
+    pp.items = (int)items;
+    pp.ring_in_stage = ring_ok ? 1 : 0;
+    int occ = 0;
+    int rc = occupancy(reinterpret_cast<const void*>(fn), pp.L.total, nssm::kPT, &occ);
+    if (rc) return rc;
+    if (occ >= target) {
+      fn<<<(unsigned)grid, nssm::kPT, pp.L.total, st>>>(pp);
+      *done = true;
+      return cuda_check("tiered_persistent_kernel launch");
+    }
+  }
+  return NSSM_OK;
+}
+
+template <int PB, int NC, int COLD, bool IOBF>
+int launch_persistent(const nssm::StepParams& sp, int batch, cudaStream_t st, bool ring_ok) {
+  const long long items = (long long)batch * sp.H;
+  if (items > (1ll << 30)) return launch_step<PB, NC, COLD, kTPR>(sp, batch, st);
+  int sms = 0;
+  int rc = sm_count(&sms);
+  if (rc) return rc;
+  bool done = false;
+  rc = launch_phase<PB, NC, COLD, IOBF, nssm::PH_STEP, 0>(sp, batch, st, ring_ok, sms, &done);
+  if (rc) return rc;
+  if (!done) return launch_step<PB, NC, COLD, kTPR>(sp, batch, st);
+  // the replay loops are unrolled for the usual flush periods of the fp8 tier
+  if (COLD == COLD_FP8 && sp.c == 4)
+    rc = launch_phase<PB, NC, COLD, IOBF, nssm::PH_FLUSH, 4>(sp, batch, st, ring_ok, sms, &done);
+  else if (COLD == COLD_FP8 && sp.c == 8)
+    rc = launch_phase<PB, NC, COLD, IOBF, nssm::PH_FLUSH, 8>(sp, batch, st, ring_ok, sms, &done);
+  else if (COLD == COLD_FP8 && sp.c == 16)
+    rc = launch_phase<PB, NC, COLD, IOBF, nssm::PH_FLUSH, 16>(sp, batch, st, ring_ok, sms, &done);
+  else
+    rc = launch_phase<PB, NC, COLD, IOBF, nssm::PH_FLUSH, 0>(sp, batch, st, ring_ok, sms, &done);
+  if (rc) return rc;
+  if (!done) return fail(NSSM_ERR_UNSUPPORTED, "flush phase does not fit this device");
+  return NSSM_OK;
+}
+
+template <int PB, int NC, int COLD>
+int launch_tiered(const nssm::StepParams& sp, int batch, cudaStream_t st) {
+  constexpr int N = PB + NC;
+  const int iob = io_bytes(sp.io_dtype);
+#ifdef NSSM_FORCE_SIMPLE
+  return launch_step<PB, NC, COLD, kTPR>(sp, batch, st);
+#endif
+  auto a16 = [](long long v) { return (v % 16) == 0; };
+  const bool tma_ok = sp.P % 4 == 0 && sp.P <= nssm::kPMaxPersistent && aligned16(sp.hot) &&
+                      aligned16(sp.cold) && (COLD != COLD_FP8 || aligned16(sp.scale)) && aligned16(sp.x) &&
+                      a16(sp.x_sb * iob) && a16(sp.x_sh * iob) && a16((long long)sp.P * iob) &&
+                      aligned16(sp.B) && aligned16(sp.C) && a16(sp.B_sb * iob) && a16(sp.C_sb * iob) &&
+                      a16((long long)N * iob);
+  if (!tma_ok) return launch_step<PB, NC, COLD, kTPR>(sp, batch, st);
+  const bool ring_ok = sp.c <= nssm::kRingInStage && aligned16(sp.ring_x) && aligned16(sp.ring_b) &&
+                       aligned16(sp.ring_dt) && a16((long long)sp.c * sp.P * iob) &&
+                       a16((long long)sp.c * NC * iob);
+  if (sp.io_dtype == NSSM_BF16) return launch_persistent<PB, NC, COLD, true>(sp, batch, st, ring_ok);
+  return launch_persistent<PB, NC, COLD, false>(sp, batch, st, ring_ok);
+}
+
+template <int PB, int NC, int COLD, int TPR>
+int launch_split(const nssm::SplitParams& sp, int batch, cudaStream_t st) {
+  dim3 grid(sp.H, batch);
+  const int threads = round_up(sp.P * TPR, 32);
+  nssm::prefill_split_kernel<PB, NC, COLD, TPR><<<grid, threads, 0, st>>>(sp);
+  return cuda_check("prefill_split_kernel launch");
+}
+
+template <int PB, int NC, int COLD, int TPR>
+int launch_mat(const nssm::MatParams& mp, int batch, cudaStream_t st) {
+  dim3 grid(mp.H, batch);
+  const int threads = round_up(mp.P * TPR, 32);
+  nssm::materialize_kernel<PB, NC, COLD, TPR><<<grid, threads, 2 * nssm::kMaxChunk * sizeof(float), st>>>(mp);
+  return cuda_check("materialize_kernel launch");
+}
+
+// Instances compiled: dstate 128, hot width 16/32/64, cold fp8/bf16/fp32.
+enum Op { OP_STEP, OP_SPLIT, OP_MAT };
+
+template <int PB, int COLD>
+int run_op(Op op, const void* params, int batch, cudaStream_t st) {
+  constexpr int NC = 128 - PB;
+  switch (op) {
+    case OP_STEP: return launch_tiered<PB, NC, COLD>(*static_cast<const nssm::StepParams*>(params), batch, st);
+    case OP_SPLIT: return launch_split<PB, NC, COLD, kTPR>(*static_cast<const nssm::SplitParams*>(params), batch, st);
+    case OP_MAT: return launch_mat<PB, NC, COLD, kTPR>(*static_cast<const nssm::MatParams*>(params), batch, st);
+  }
+  return fail(NSSM_ERR_INVALID, "unknown op");
+}
+
+template <int PB>
+int run_cold(Op op, int cold, const void* params, int batch, cudaStream_t st) {
+  switch (cold) {
+    case NSSM_F8E4M3: return run_op<PB, COLD_FP8>(op, params, batch, st);
+    case NSSM_BF16: return run_op<PB, COLD_BF16>(op, params, batch, st);
+    case NSSM_F32: return run_op<PB, COLD_F32>(op, params, batch, st);
+  }
+  return fail(NSSM_ERR_INVALID, "cold_dtype %d is not one of F32/BF16/F8E4M3", cold);
+}
+
+int dispatch(Op op, int N, int pb, int cold, const void* params, int batch, cudaStream_t st) {
+  if (N != 128) return fail(NSSM_ERR_UNSUPPORTED, "dstate %d not compiled (supported: 128)", N);
+  switch (pb) {
+    case 16: return run_cold<16>(op, cold, params, batch, st);
+    case 32: return run_cold<32>(op, cold, params, batch, st);
+    case 64: return run_cold<64>(op, cold, params, batch, st);
+  }
+  return fail(NSSM_ERR_UNSUPPORTED, "hot_dim %d not compiled for dstate %d (supported: 16, 32, 64)", pb, N);
+}
+
+// ---- validation ---------------------------------------------------------
+int check_pool(const nssm_pool* pl) {
+  if (!pl) return fail(NSSM_ERR_INVALID, "pool is NULL");
+  if (pl->num_slots <= 0 || pl->nheads <= 0 || pl->headdim <= 0 || pl->dstate <= 0 || pl->ngroups <= 0)
+    return fail(NSSM_ERR_INVALID, "pool dims must be positive (S=%d H=%d P=%d N=%d G=%d)", pl->num_slots,
+                pl->nheads, pl->headdim, pl->dstate, pl->ngroups);
+  if (pl->nheads % pl->ngroups) return fail(NSSM_ERR_INVALID, "nheads %d not divisible by ngroups %d", pl->nheads, pl->ngroups);
+  if (pl->hot_dim <= 0 || pl->hot_dim >= pl->dstate)
+    return fail(NSSM_ERR_INVALID, "hot_dim %d must be in [1, dstate) (use nssm_fresh_step for an all-hot state)", pl->hot_dim);
+  if (pl->chunk < 1 || pl->chunk > nssm::kMaxChunk)
+    return fail(NSSM_ERR_INVALID, "chunk %d outside [1, %d]", pl->chunk, nssm::kMaxChunk);
+  if (pl->headdim * kTPR > 128 * kTPR) return fail(NSSM_ERR_UNSUPPORTED, "headdim %d > 128", pl->headdim);
+  if (pl->io_dtype != NSSM_F32 && pl->io_dtype != NSSM_BF16)
+    return fail(NSSM_ERR_INVALID, "io_dtype %d must be F32 or BF16", pl->io_dtype);
+  if (!pl->hot || !pl->cold || !pl->glog || !pl->t || !pl->ring_x || !pl->ring_dt || !pl->ring_b)
+    return fail(NSSM_ERR_INVALID, "a pool buffer is NULL");
+  if (pl->cold_dtype == NSSM_F8E4M3 && !pl->cold_scale) return fail(NSSM_ERR_INVALID, "fp8 cold needs cold_scale");
+  if (!aligned16(pl->hot) || !aligned16(pl->cold) || (pl->cold_scale && !aligned16(pl->cold_scale)))
+    return fail(NSSM_ERR_INVALID, "hot / cold / cold_scale must be 16-byte aligned");
+  return NSSM_OK;
+}
+
+int check_args(const nssm_step_args* a, int H) {
+  if (!a) return fail(NSSM_ERR_INVALID, "args is NULL");
+  if (a->batch < 0) return fail(NSSM_ERR_INVALID, "batch %d < 0", a->batch);
+  if (a->batch > 65535) return fail(NSSM_ERR_UNSUPPORTED, "batch %d > 65535 rows per call", a->batch);
+  if (!a->x || !a->dt || !a->A || !a->B || !a->C || !a->out) return fail(NSSM_ERR_INVALID, "x/dt/A/B/C/out must be non-NULL");
+  if (a->io_dtype != NSSM_F32 && a->io_dtype != NSSM_BF16) return fail(NSSM_ERR_INVALID, "io_dtype must be F32 or BF16");
+  if (a->dt_dtype != NSSM_F32 && a->dt_dtype != NSSM_BF16) return fail(NSSM_ERR_INVALID, "dt_dtype must be F32 or BF16");
+  if (a->out_dtype != NSSM_F32 && a->out_dtype != NSSM_BF16) return fail(NSSM_ERR_INVALID, "out_dtype must be F32 or BF16");
+  if (a->mode < NSSM_MODE_STALE || a->mode > NSSM_MODE_COLDOFF) return fail(NSSM_ERR_INVALID, "mode %d unknown", a->mode);
+  (void)H;
+  return NSSM_OK;
+}
+
+// The rotation kernel stages R[g] (66 KB) in shared memory: opt in once per device.
+int ensure_rot_attr(size_t smem) {
+  static std::atomic<uint64_t> done{0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return cuda_check("cudaGetDevice");
+  const uint64_t bit = 1ull << (dev & 63);
+  if (done.load(std::memory_order_acquire) & bit) return NSSM_OK;
+  if (cudaFuncSetAttribute(nssm::rot_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return cuda_check("cudaFuncSetAttribute(rot_kernel)");
+  done.fetch_or(bit, std::memory_order_acq_rel);
+  return NSSM_OK;
+}
+
+// Rotate B and C into the workspace (if R given); fills sp.B / sp.C.
+int maybe_rotate(const nssm_step_args* a, int G, int N, nssm::StepParams& sp, cudaStream_t st) {
+  sp.B = a->B; sp.B_sb = a->B_stride_b;
+  sp.C = a->C; sp.C_sb = a->C_stride_b;
+  if (!a->R || a->batch == 0) return NSSM_OK;
+  const size_t need = nssm_step_workspace_bytes(a->batch, G, N, a->io_dtype, 1);
+  if (!a->workspace || a->workspace_bytes < need)
+    return fail(NSSM_ERR_INVALID, "workspace of %zu bytes needed for the rotation (got %zu)", need, a->workspace_bytes);
+  if (N != 128) return fail(NSSM_ERR_UNSUPPORTED, "rotation compiled for dstate 128 only");
+  const size_t half = need / 2;
+  int rc0;
+  nssm::RotParams rp{};
+  rp.x0 = a->B; rp.xs0 = a->B_stride_b;
+  rp.x1 = a->C; rp.xs1 = a->C_stride_b;
+  rp.o0 = a->workspace; rp.os0 = (int64_t)G * N;
+  rp.o1 = static_cast<char*>(a->workspace) + half; rp.os1 = (int64_t)G * N;
+  rp.R = a->R; rp.T = a->batch; rp.G = G; rp.dtype = a->io_dtype;
+  rp.idx = a->state_batch_indices; rp.pad = a->pad_slot_id;
+  const size_t smem = sizeof(float) * (128 * 129 + nssm::kRotRows * 128);
+  rc0 = ensure_rot_attr(smem);
+  if (rc0) return rc0;
+  dim3 grid((a->batch + nssm::kRotRows - 1) / nssm::kRotRows, G, 2);
+  nssm::rot_kernel<128><<<grid, 128, smem, st>>>(rp);
+  int rc = cuda_check("rot_kernel launch");
+  if (rc) return rc;
+  sp.B = rp.o0; sp.B_sb = rp.os0;
+  sp.C = rp.o1; sp.C_sb = rp.os1;
+  return NSSM_OK;
+}
+
+void fill_inputs(const nssm_step_args* a, nssm::StepParams& sp) {
+  sp.x = a->x; sp.x_sb = a->x_stride_b; sp.x_sh = a->x_stride_h;
+  sp.dt = a->dt; sp.dt_sb = a->dt_stride_b; sp.dt_sh = a->dt_stride_h; sp.dt_dtype = a->dt_dtype;
+  sp.softplus = a->dt_softplus;
+  sp.io_dtype = a->io_dtype;
+  sp.A = a->A; sp.D = a->D; sp.dt_bias = a->dt_bias; sp.dt_min = a->dt_min;
+  sp.mode = a->mode;
+  sp.idx = a->state_batch_indices; sp.pad = a->pad_slot_id;
+  sp.out = a->out; sp.out_sb = a->out_stride_b; sp.out_sh = a->out_stride_h; sp.out_dtype = a->out_dtype;
+  sp.status = a->status;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t nssm_step_workspace_bytes(int32_t batch, int32_t ngroups, int32_t dstate, int32_t io_dtype,
+                                 int32_t has_rotation) {
+  if (!has_rotation || batch <= 0) return 0;
+  size_t half = (size_t)batch * ngroups * dstate * io_bytes(io_dtype);
+  half = (half + 255) / 256 * 256;
+  return 2 * half;
+}
+
+int nssm_tiered_step(const nssm_pool* pool, const nssm_step_args* args, void* stream) {
+  int rc = check_pool(pool);
+  if (rc) return rc;
+  rc = check_args(args, pool->nheads);
+  if (rc) return rc;
+  if (args->io_dtype != pool->io_dtype)
+    return fail(NSSM_ERR_INVALID, "args io_dtype %d differs from the pool's ring dtype %d", args->io_dtype, pool->io_dtype);
+  if (args->batch == 0) return NSSM_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  nssm::StepParams sp{};
+  sp.hot = pool->hot; sp.cold = pool->cold; sp.scale = pool->cold_scale;
+  sp.glog = pool->glog; sp.t = pool->t;
+  sp.ring_x = pool->ring_x; sp.ring_dt = pool->ring_dt; sp.ring_b = pool->ring_b;
+  sp.S = pool->num_slots; sp.H = pool->nheads; sp.P = pool->headdim; sp.G = pool->ngroups; sp.c = pool->chunk;
+  fill_inputs(args, sp);
+  rc = maybe_rotate(args, pool->ngroups, pool->dstate, sp, st);
+  if (rc) return rc;
+  return dispatch(OP_STEP, pool->dstate, pool->hot_dim, pool->cold_dtype, &sp, args->batch, st);
+}
+
+int nssm_fresh_step(float* state, int32_t num_slots, int32_t nheads, int32_t headdim, int32_t dstate,
+                    int32_t ngroups, const nssm_step_args* args, void* stream) {
+  if (!state) return fail(NSSM_ERR_INVALID, "state is NULL");
+  if (!aligned16(state)) return fail(NSSM_ERR_INVALID, "state must be 16-byte aligned");
+  if (num_slots <= 0 || nheads <= 0 || headdim <= 0 || ngroups <= 0 || nheads % ngroups)
+    return fail(NSSM_ERR_INVALID, "bad dims (S=%d H=%d P=%d G=%d)", num_slots, nheads, headdim, ngroups);
+  if (dstate != 128) return fail(NSSM_ERR_UNSUPPORTED, "fresh step compiled for dstate 128 only");
+  if (headdim > 128) return fail(NSSM_ERR_UNSUPPORTED, "headdim %d > 128", headdim);
+  int rc = check_args(args, nheads);
+  if (rc) return rc;
+  if (args->batch == 0) return NSSM_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  nssm::StepParams sp{};
+  sp.hot = state;
+  sp.S = num_slots; sp.H = nheads; sp.P = headdim; sp.G = ngroups; sp.c = 1;
+  fill_inputs(args, sp);
+  sp.mode = NSSM_MODE_STALE;
+  rc = maybe_rotate(args, ngroups, dstate, sp, st);
+  if (rc) return rc;
+  dim3 grid(nheads, args->batch);
+  const int threads = round_up(headdim * kTPRFresh, 32);
+  nssm::tiered_step_kernel<128, 0, COLD_NONE, kTPRFresh><<<grid, threads, step_smem_bytes<128, 0, COLD_NONE>(headdim, 1), st>>>(sp);
+  return cuda_check("fresh step launch");
+}
+
+int nssm_prefill_split(const nssm_pool* pool, const float* state, int64_t state_stride_b, const int32_t* slots,
+                       int32_t batch, int32_t pad_slot_id, void* stream) {
+  int rc = check_pool(pool);
+  if (rc) return rc;
+  if (batch < 0 || batch > 65535) return fail(NSSM_ERR_INVALID, "batch %d outside [0, 65535]", batch);
+  if (batch == 0) return NSSM_OK;
+  if (!state) return fail(NSSM_ERR_INVALID, "state is NULL");
+  if (!aligned16(state) || (state_stride_b % 4)) return fail(NSSM_ERR_INVALID, "state rows must be 16-byte aligned");
+  nssm::SplitParams sp{};
+  sp.hot = pool->hot; sp.cold = pool->cold; sp.scale = pool->cold_scale; sp.glog = pool->glog; sp.t = pool->t;
+  sp.S = pool->num_slots; sp.H = pool->nheads; sp.P = pool->headdim;
+  sp.src = state; sp.src_sb = state_stride_b; sp.idx = slots; sp.pad = pad_slot_id; sp.status = nullptr;
+  return dispatch(OP_SPLIT, pool->dstate, pool->hot_dim, pool->cold_dtype, &sp, batch, static_cast<cudaStream_t>(stream));
+}
+
+int nssm_materialize(const nssm_pool* pool, const float* A, const int32_t* slots, int32_t batch,
+                     int32_t pad_slot_id, float* out, int64_t out_stride_b, void* stream) {
+  int rc = check_pool(pool);
+  if (rc) return rc;
+  if (batch < 0 || batch > 65535) return fail(NSSM_ERR_INVALID, "batch %d outside [0, 65535]", batch);
+  if (batch == 0) return NSSM_OK;
+  if (!A || !out) return fail(NSSM_ERR_INVALID, "A / out is NULL");
+  if (!aligned16(out) || (out_stride_b % 4)) return fail(NSSM_ERR_INVALID, "out rows must be 16-byte aligned");
+  nssm::MatParams mp{};
+  mp.hot = pool->hot; mp.cold = pool->cold; mp.scale = pool->cold_scale; mp.t = pool->t;
+  mp.ring_x = pool->ring_x; mp.ring_dt = pool->ring_dt; mp.ring_b = pool->ring_b;
+  mp.S = pool->num_slots; mp.H = pool->nheads; mp.P = pool->headdim; mp.G = pool->ngroups; mp.c = pool->chunk;
+  mp.io_dtype = pool->io_dtype; mp.A = A; mp.idx = slots; mp.pad = pad_slot_id; mp.out = out; mp.out_sb = out_stride_b;
+  mp.status = nullptr;
+  return dispatch(OP_MAT, pool->dstate, pool->hot_dim, pool->cold_dtype, &mp, batch, static_cast<cudaStream_t>(stream));
+}
+
+int nssm_rot_flat(const void* x, int64_t x_stride, int32_t dtype, const float* R, int32_t T, int32_t ngroups,
+                  int32_t dstate, void* out, int64_t out_stride, void* stream) {
+  if (T < 0 || T > 65535 * nssm::kRotRows) return fail(NSSM_ERR_INVALID, "T %d out of range", T);
+  if (T == 0) return NSSM_OK;
+  if (!x || !R || !out) return fail(NSSM_ERR_INVALID, "x / R / out is NULL");
+  if (dtype != NSSM_F32 && dtype != NSSM_BF16) return fail(NSSM_ERR_INVALID, "dtype must be F32 or BF16");
+  if (dstate != 128) return fail(NSSM_ERR_UNSUPPORTED, "rotation compiled for dstate 128 only");
+  if (ngroups <= 0) return fail(NSSM_ERR_INVALID, "ngroups %d", ngroups);
+  nssm::RotParams rp{};
+  rp.x0 = rp.x1 = x; rp.xs0 = rp.xs1 = x_stride;
+  rp.o0 = rp.o1 = out; rp.os0 = rp.os1 = out_stride;
+  rp.R = R; rp.T = T; rp.G = ngroups; rp.dtype = dtype; rp.idx = nullptr; rp.pad = -1;
+  const size_t smem = sizeof(float) * (128 * 129 + nssm::kRotRows * 128);
+  int rc = ensure_rot_attr(smem);
+  if (rc) return rc;
+  dim3 grid((T + nssm::kRotRows - 1) / nssm::kRotRows, ngroups, 1);
+  nssm::rot_kernel<128><<<grid, 128, smem, static_cast<cudaStream_t>(stream)>>>(rp);
+  return cuda_check("rot_kernel launch");
+}
+
+int32_t nssm_supported_hot_dims(int32_t dstate, int32_t* widths, int32_t cap) {
+  static const int32_t k128[] = {16, 32, 64};
+  if (dstate != 128) return 0;
+  int32_t n = 0;
+  for (int32_t w : k128) {
+    if (widths && n < cap) widths[n] = w;
+    ++n;
+  }
+  return n;
+}
+
+size_t nssm_sizeof_pool(void) { return sizeof(nssm_pool); }
+size_t nssm_sizeof_step_args(void) { return sizeof(nssm_step_args); }
+int32_t nssm_abi_version(void) { return NSSM_ABI_VERSION; }
+const char* nssm_last_error(void) { return g_last_error.c_str(); }
+
+}  // extern "C"

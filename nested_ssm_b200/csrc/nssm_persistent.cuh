@@ -1,0 +1,785 @@
+// Persistent, TMA-pipelined kernels of the tiered step (sm_100a): the per-token
+// STEP phase (hot update, stale readout, ring write, bookkeeping) and the FLUSH
+// phase (rank-c replay of the ring into the cold slice + requantisation) of the
+// slots whose token count reached a multiple of c.  A step launches STEP, then
+// FLUSH on the same stream; FLUSH finds its work from the token counts STEP wrote.
+//
+// Grid = (#SMs x resident CTAs).  CTA k owns the contiguous range of work items
+// [k*W/G, (k+1)*W/G) over (batch row, head), W = batch*H, so it streams the tiles of
+// consecutive heads of the same slot.
+//
+// Prologue (once per CTA): the slot and token count of every batch row in range and
+// (STEP) every item's scalars (dt = softplus(dt_raw + dt_bias) clamped, dt*A,
+// exp(dt*A), exp(glog), D) are computed in parallel into shared memory.
+//
+// Main loop: one elected thread keeps kStages items in flight with 1-D bulk copies
+// (cp.async.bulk global->shared, no multicast) completing on a "full" mbarrier per
+// stage.  Every warp owns a fixed band of headdim rows of every item, so row sums,
+// the y pass, the replay and the row amax of the requantisation are warp-local: no
+// CTA-wide barrier in the steady state.  A warp releases a stage by arriving on its
+// "empty" mbarrier; the producer refills the stage once all warps arrived.
+//
+// Inside a band the tile is read in 16-byte chunks, consecutive lanes on
+// consecutive chunks (conflict-free shared-memory reads, coalesced write-back).
+#pragma once
+
+#include "nssm_device.cuh"
+
+// Pipeline depth, CTA size and resident CTAs per SM of the persistent kernels.
+#ifndef NSSM_STEP_STAGES
+#define NSSM_STEP_STAGES 3
+#endif
+#ifndef NSSM_FLUSH_STAGES
+#define NSSM_FLUSH_STAGES 8
+#endif
+#ifndef NSSM_PTHREADS
+#define NSSM_PTHREADS 256
+#endif
+#ifndef NSSM_STEP_P_MINB
+#define NSSM_STEP_P_MINB 3
+#endif
+#ifndef NSSM_FLUSH_P_MINB
+#define NSSM_FLUSH_P_MINB 2
+#endif
+
+namespace nssm {
+
+constexpr int kMaxStages = NSSM_STEP_STAGES > NSSM_FLUSH_STAGES ? NSSM_STEP_STAGES : NSSM_FLUSH_STAGES;
+__host__ __device__ constexpr int stages_for(int phase) { return phase == 0 ? NSSM_STEP_STAGES : NSSM_FLUSH_STAGES; }
+constexpr int kPT = NSSM_PTHREADS;         // threads per CTA
+constexpr int kPW = kPT / 32;              // warps per CTA
+constexpr int kPMaxPersistent = 80;        // headdim bound of the persistent path (10 rows per warp)
+constexpr int kRingInStage = 16;           // c up to this: the ring rides in the stage
+constexpr int kRingF32Max = 8;             // c up to this: each warp keeps the ring B as fp32
+constexpr uint32_t kSpinLimit = 1u << 26;  // bounded mbarrier wait, then error + exit
+enum : int { STATUS_TIMEOUT = 2 };
+enum : int { PH_STEP = 0, PH_FLUSH = 1 };
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// 1-D bulk copy global -> this CTA's shared memory (16-byte aligned, size % 16 == 0)
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+// 1-D bulk copy this CTA's shared memory -> global (16-byte aligned, size % 16 == 0)
+__device__ __forceinline__ void bulk_s2g(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(smem_u32(src)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// the shared-memory sources of all committed bulk stores have been read
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// all committed bulk stores are complete
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait; false on timeout.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+  for (uint32_t it = 0; it < kSpinLimit; ++it)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+
+// Correctly rounded a / b given r = RN(1/b) (Markstein's FMA correction:
+// q0 = RN(a r) is within one ulp of a/b, the residual a - b q0 is exact in one FMA,
+// and RN(q0 + residual * r) is the correctly rounded quotient, barring underflow).
+__device__ __forceinline__ float div_rn_fma(float a, float b, float r) {
+  const float q0 = __fmul_rn(a, r);
+  const float e = __fmaf_rn(-q0, b, a);
+  return __fmaf_rn(e, r, q0);
+}
+
+// Byte layout of the dynamic shared memory (computed on the host, passed in).
+struct PLayout {
+  int stage_bytes;
+  int s_hot, s_cold, s_scale, s_x, s_b, s_c, s_rx, s_rb, s_rdt;   // inside a stage (0 size if unused)
+  int off_scal, off_head, off_yh, off_pc, off_sc, off_rcp, off_wsc, off_sw, off_rbw, off_fsc, off_bslot, off_bmeta,
+      off_bpos, off_bar;
+  int total;
+  int rpw;          // headdim rows per warp band
+  int wsc_stride;   // floats of per-warp scratch (suffix decays / corr weights)
+  int maxb;         // batch rows one CTA can touch
+  int maxitems;     // items one CTA can own
+};
+
+__host__ __device__ inline int al(int v, int a) { return (v + a - 1) / a * a; }
+
+constexpr int kScal = 8;   // per-item scalars (STEP): dt, dA, exp(dA), exp(glog), glog, D, A, -
+
+template <int PB, int NC, int COLD>
+__host__ inline PLayout make_playout(int phase, bool corr, int P, int H, int c, int io_bytes, int maxb,
+                                     int maxitems, bool ring_in_stage) {
+  constexpr int N = PB + NC;
+  constexpr int ESZ = ColdTraits<COLD>::kBytes;
+  constexpr int CPR = (NC * ESZ) / 16;
+  const bool step = phase == PH_STEP;
+  const bool ring = ring_in_stage && (!step || corr);
+  PLayout L{};
+  int o = 0;
+  L.s_hot = o; o = al(o + (step ? P * PB * 4 : 0), 128);
+  L.s_cold = o; o = al(o + P * NC * ESZ, 128);
+  L.s_scale = o; o = al(o + (COLD == COLD_FP8 ? P * 4 : 0), 16);
+  L.s_x = o; o = al(o + (step ? P * io_bytes : 0), 16);
+  L.s_b = o; o = al(o + (step ? N * io_bytes : 0), 16);
+  L.s_c = o; o = al(o + (step ? N * io_bytes : 0), 16);
+  L.s_rx = o; o = al(o + (ring ? c * P * io_bytes : 0), 16);
+  L.s_rb = o; o = al(o + (ring ? c * NC * 4 : 0), 16);      // ring B is fp32
+  L.s_rdt = o; o = al(o + (ring ? ring_dt_stride(c) * 4 : 0), 16);
+  L.stage_bytes = al(o, 128);
+  L.rpw = (P + kPW - 1) / kPW;
+  L.wsc_stride = al(2 * c + 2, 4);
+  const int nst = stages_for(phase);
+  int t = nst * L.stage_bytes;
+  L.off_scal = t; t += (step ? maxitems * kScal * 4 : 0);
+  L.off_head = t; t += H * 4;                    // A per head (FLUSH)
+  L.off_yh = t; t += P * 4;
+  L.off_pc = t; t += P * CPR * 4;
+  L.off_sc = t; t += P * 4;
+  L.off_rcp = t; t += P * 4;
+  L.off_wsc = t; t += kPW * L.wsc_stride * 4;
+  L.off_sw = t; t += (step ? 0 : c * P * 4);     // flush weights W_j[row] (rows are warp-private)
+  L.off_rbw = t;
+  // per-item suffix decays of the flush: exp(suf_j) [c], dt_j [c], exp(total)
+  L.off_fsc = t; t += (!step && c <= kRingF32Max) ? maxitems * (2 * c + 1) * 4 : 0;
+  L.off_bslot = t; t += maxb * 4;
+  L.off_bmeta = t; t += maxb * 4;
+  L.off_bpos = t; t += maxb * 4;
+  t = al(t, 8);
+  L.off_bar = t; t += 2 * nst * 8;               // full[stages], empty[stages]
+  L.total = al(t, 128);
+  L.maxb = maxb;
+  L.maxitems = maxitems;
+  return L;
+}
+
+struct PParams {
+  StepParams sp;
+  PLayout L;
+  int items;          // batch * H
+  int ring_in_stage;  // the ring rides in the stage (c <= kRingInStage, aligned)
+};
+
+__device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
+
+// e4m3 byte s|eeee|mmm placed at f32 bits 31|26..23|22..20 is exactly q * 2^-120,
+// subnormals and zero included (the f32 exponent field 0000eeee is the e4m3 one
+// re-biased by 120): four values per word from integer shifts and masks only.
+constexpr float kTwo120 = 1.329227995784915872903807060280344576e36f;   // 2^120
+__device__ __forceinline__ void fp8x4_scaled(uint32_t w, float* v) {
+  v[0] = __int_as_float((static_cast<int>(w << 24) >> 4) & static_cast<int>(0x87F00000u));
+  v[1] = __int_as_float((static_cast<int>(w << 16) >> 4) & static_cast<int>(0x87F00000u));
+  v[2] = __int_as_float((static_cast<int>(w << 8) >> 4) & static_cast<int>(0x87F00000u));
+  v[3] = __int_as_float((static_cast<int>(w) >> 4) & static_cast<int>(0x87F00000u));
+}
+
+template <bool IOBF>
+__device__ __forceinline__ float ldv(const void* p, int64_t i) {
+  if constexpr (IOBF) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+  else return reinterpret_cast<const float*>(p)[i];
+}
+template <bool IOBF>
+__device__ __forceinline__ void stv(void* p, int64_t i, float v) {
+  if constexpr (IOBF) reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+  else reinterpret_cast<float*>(p)[i] = v;
+}
+
+// CNT consecutive io values starting at element n0 of a shared row, as fp32.
+template <int CNT, bool IOBF>
+__device__ __forceinline__ void ld_row(const unsigned char* row, int n0, float* v) {
+  if constexpr (IOBF) {
+    const unsigned char* s = row + n0 * 2;
+    if constexpr (CNT % 8 == 0) {
+#pragma unroll
+      for (int q = 0; q < CNT / 8; ++q) {
+        const uint4 w = reinterpret_cast<const uint4*>(s)[q];
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          v[8 * q + 2 * k] = __uint_as_float(ws[k] << 16);
+          v[8 * q + 2 * k + 1] = __uint_as_float(ws[k] & 0xffff0000u);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < CNT / 2; ++q) {
+        const uint32_t w = reinterpret_cast<const uint32_t*>(s)[q];
+        v[2 * q] = __uint_as_float(w << 16);
+        v[2 * q + 1] = __uint_as_float(w & 0xffff0000u);
+      }
+    }
+  } else {
+    const float4* s = reinterpret_cast<const float4*>(row + n0 * 4);
+#pragma unroll
+    for (int q = 0; q < CNT / 4; ++q) {
+      const float4 w = s[q];
+      v[4 * q] = w.x; v[4 * q + 1] = w.y; v[4 * q + 2] = w.z; v[4 * q + 3] = w.w;
+    }
+  }
+}
+
+// CFIX > 0 compiles the kernel for that flush period (unrolled replay loops);
+// 0 takes c from the parameters.
+template <int PB, int NC, int COLD, bool IOBF, int PHASE, int CFIX>
+__global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSSM_FLUSH_P_MINB)
+    tiered_persistent_kernel(const __grid_constant__ PParams pp) {
+  using Sh = StepShape<PB, NC, COLD>;
+  constexpr int N = Sh::N;
+  constexpr int LPR = Sh::LPR;     // hot 16-byte chunks per row
+  constexpr int CPR = Sh::CPR;     // cold 16-byte chunks per row
+  constexpr int CE = Sh::CE;       // cold elements per chunk
+  constexpr int ESZ = Sh::ESZ;
+  constexpr int kPerW = WordTraits<COLD>::kPer;
+  constexpr int IOB = IOBF ? 2 : 4;
+  constexpr bool STEP = PHASE == PH_STEP;
+  constexpr int kStages = stages_for(PHASE);
+  constexpr int RPWMAX = (kPMaxPersistent + kPW - 1) / kPW;   // rows per warp band
+  constexpr int HQ = (RPWMAX * LPR + 31) / 32;                // hot chunks per lane
+  constexpr int CQ = (RPWMAX * CPR + 31) / 32;                // cold chunks per lane (STEP)
+  constexpr int CQF = (CPR + (32 / RPWMAX) - 1) / (32 / RPWMAX);   // column passes (FLUSH)
+  static_assert(32 % LPR == 0, "hot row chunks must tile a warp");
+  static_assert(COLD != COLD_NONE && NC > 0, "tiered instances only");
+  static_assert(CE % 4 == 0 && PB % 4 == 0, "chunk shapes");
+
+  const StepParams& p = pp.sp;
+  const PLayout& L = pp.L;
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int c = CFIX > 0 ? CFIX : p.c;
+  const int Pn = p.P;
+  const int H = p.H;
+  const int cp = ring_dt_stride(c);
+  const int HG = H / p.G;
+  const bool corr = (p.mode == NSSM_MODE_CORR);
+  const bool ring_st = pp.ring_in_stage != 0 && (!STEP || corr);
+
+  extern __shared__ __align__(128) unsigned char sm[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + L.off_bar);
+  uint64_t* empty = full + kStages;
+  const float* scal = reinterpret_cast<const float*>(sm + L.off_scal);
+  float* sA = reinterpret_cast<float*>(sm + L.off_head);
+  float* yh = reinterpret_cast<float*>(sm + L.off_yh);
+  float* pc = reinterpret_cast<float*>(sm + L.off_pc);
+  float* s_sc = reinterpret_cast<float*>(sm + L.off_sc);
+  float* s_rcp = reinterpret_cast<float*>(sm + L.off_rcp);
+  float* wsc = reinterpret_cast<float*>(sm + L.off_wsc) + warp * L.wsc_stride;   // per-warp scratch
+  float* sW = reinterpret_cast<float*>(sm + L.off_sw);
+  int* bslot = reinterpret_cast<int*>(sm + L.off_bslot);
+  int* btn = reinterpret_cast<int*>(sm + L.off_bmeta);   // token count after this step
+  int* bpos = reinterpret_cast<int*>(sm + L.off_bpos);   // ring position of this token, -(pos+1) if it flushes
+
+  const int W = pp.items;
+  const int beg = (int)((long long)W * blockIdx.x / gridDim.x);
+  const int end = (int)((long long)W * (blockIdx.x + 1) / gridDim.x);
+  if (beg >= end) return;
+  const int b0 = beg / H;
+  const int nb = (end - 1) / H - b0 + 1;
+  const int nit = end - beg;
+
+  // ---- prologue 1: slot and token count after this step of every batch row in
+  // range.  STEP reads t and adds one; FLUSH reads the count STEP wrote and keeps
+  // only the rows that flush.
+  for (int j = tid; j < nb; j += kPT) {
+    const int b = b0 + j;
+    const int slot = p.idx ? p.idx[b] : b;
+    int s = -1, tn = 0;
+    if (slot != p.pad) {
+      if (slot < 0 || slot >= p.S) {
+        if (STEP && p.status) atomicOr(p.status, STATUS_BAD_SLOT);
+      } else {
+        const int hf = (j == 0) ? beg - b0 * H : 0;   // first head of row b owned here
+        s = slot;
+        tn = p.t[(int64_t)slot * H + hf] + (STEP ? 1 : 0);
+        if (!STEP && (tn <= 0 || tn % c != 0)) s = -1;   // FLUSH: only flushing rows
+      }
+    }
+    bslot[j] = s;
+    btn[j] = tn;
+    const int ps = tn > 0 ? (tn - 1) % c : 0;
+    bpos[j] = (ps == c - 1) ? -(ps + 1) : ps;
+  }
+  if (!STEP) {
+    for (int h = tid; h < H; h += kPT) sA[h] = p.A[h];
+  }
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kPW);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  // ---- prologue 2 (STEP): every item's scalars, in parallel
+  if constexpr (STEP) {
+    for (int it = tid; it < nit; it += kPT) {
+      const int w = beg + it;
+      const int b = w / H, h = w - (w / H) * H;
+      const int slot = bslot[b - b0];
+      if (slot < 0) continue;
+      float d = ld_io(p.dt, (int64_t)b * p.dt_sb + (int64_t)h * p.dt_sh, p.dt_dtype);
+      if (p.dt_bias) d += p.dt_bias[h];
+      if (p.softplus) d = softplus_f(d);
+      if (p.dt_min > 0.0f) d = fmaxf(d, p.dt_min);
+      const float dA = d * p.A[h];
+      const float gl = p.glog[(int64_t)slot * H + h];
+      float* f = reinterpret_cast<float*>(sm + L.off_scal) + it * kScal;
+      f[0] = d;
+      f[1] = dA;
+      f[2] = expf(dA);
+      f[3] = expf(corr ? gl + dA : gl);   // corr reads G_t inclusive
+      f[4] = gl;
+      f[5] = p.D ? p.D[h] : 0.0f;
+      f[6] = p.A[h];
+    }
+  }
+
+  // ---- prologue 2 (FLUSH): every flushing item's suffix decays, in parallel (same
+  // sequential order as the oracle: total and suffix sums accumulated j-wise)
+  if constexpr (!STEP) {
+    if (c <= kRingF32Max) {
+      for (int it = tid; it < nit; it += kPT) {
+        const int w = beg + it;
+        const int b = w / H, h = w - (w / H) * H;
+        const int slot = bslot[b - b0];
+        if (slot < 0) continue;
+        const float* rd = p.ring_dt + ((int64_t)slot * H + h) * cp;
+        const float A_h = p.A[h];
+        float dts[kRingF32Max];
+#pragma unroll
+        for (int j = 0; j < kRingF32Max; ++j) dts[j] = (j < c) ? rd[j] : 0.0f;
+        float* fs = reinterpret_cast<float*>(sm + L.off_fsc) + it * (2 * c + 1);
+        float tot = 0.0f;
+#pragma unroll
+        for (int j = 0; j < kRingF32Max; ++j)
+          if (j < c) tot = tot + dts[j] * A_h;
+        fs[2 * c] = expf(tot);
+        float suf = 0.0f;
+        fs[c - 1] = 1.0f;
+        fs[2 * c - 1] = dts[c - 1];
+#pragma unroll
+        for (int j = kRingF32Max - 2; j >= 0; --j) {
+          if (j <= c - 2) {
+            suf = suf + dts[j + 1] * A_h;
+            fs[j] = expf(suf);
+            fs[c + j] = dts[j];
+          }
+        }
+      }
+    }
+  }
+
+  // item cursor over valid items: (b, h, group, head-in-group) advanced incrementally
+  struct Cur { int b, h, g, hr; };
+  auto first_valid = [&](Cur& q) {
+    while (q.b * H + q.h < end && bslot[q.b - b0] < 0) { ++q.b; q.h = 0; q.g = 0; q.hr = 0; }
+  };
+  auto advance = [&](Cur& q) {
+    ++q.h;
+    if (++q.hr == HG) { q.hr = 0; ++q.g; }
+    if (q.h == H) { q.h = 0; q.g = 0; q.hr = 0; ++q.b; }
+    first_valid(q);
+  };
+  const int h_beg = beg - b0 * H;
+  const Cur start{b0, h_beg, h_beg / HG, h_beg % HG};
+
+  // ---- producer: bulk copies of item q into stage s (one thread)
+  auto issue = [&](const Cur& q, int s) {
+    const int j = q.b - b0, b = q.b, h = q.h, g = q.g;
+    const int slot = bslot[j];
+    const int64_t sh = (int64_t)slot * H + h;
+    unsigned char* st = sm + s * L.stage_bytes;
+    uint32_t bytes = (uint32_t)(Pn * NC * ESZ);
+    if (COLD == COLD_FP8) bytes += Pn * 4;
+    if (STEP) bytes += (uint32_t)(Pn * PB * 4 + Pn * IOB + 2 * N * IOB);
+    if (ring_st) bytes += (uint32_t)(c * Pn * IOB + c * NC * 4 + cp * 4);
+    mbar_expect_tx(&full[s], bytes);
+    bulk_g2s(st + L.s_cold, static_cast<const char*>(p.cold) + sh * Pn * NC * ESZ, Pn * NC * ESZ, &full[s]);
+    if (COLD == COLD_FP8) bulk_g2s(st + L.s_scale, p.scale + sh * Pn, Pn * 4, &full[s]);
+    if (STEP) {
+      bulk_g2s(st + L.s_hot, p.hot + sh * Pn * PB, Pn * PB * 4, &full[s]);
+      bulk_g2s(st + L.s_x, static_cast<const char*>(p.x) + ((int64_t)b * p.x_sb + (int64_t)h * p.x_sh) * IOB,
+               Pn * IOB, &full[s]);
+      bulk_g2s(st + L.s_b, static_cast<const char*>(p.B) + ((int64_t)b * p.B_sb + (int64_t)g * N) * IOB,
+               N * IOB, &full[s]);
+      bulk_g2s(st + L.s_c, static_cast<const char*>(p.C) + ((int64_t)b * p.C_sb + (int64_t)g * N) * IOB,
+               N * IOB, &full[s]);
+    }
+    if (ring_st) {
+      bulk_g2s(st + L.s_rx, static_cast<const char*>(p.ring_x) + sh * c * Pn * IOB, c * Pn * IOB, &full[s]);
+      bulk_g2s(st + L.s_rb, p.ring_b + ((int64_t)slot * p.G + g) * c * NC, c * NC * 4, &full[s]);
+      bulk_g2s(st + L.s_rdt, p.ring_dt + sh * cp, cp * 4, &full[s]);
+    }
+  };
+
+  // ---- pipeline fill
+  Cur pq = start;
+  first_valid(pq);
+  uint32_t n_issued = 0;
+  if (tid == 0) {
+    for (int s = 0; s < kStages && pq.b * H + pq.h < end; ++s) {
+      issue(pq, s);
+      ++n_issued;
+      advance(pq);
+    }
+  }
+  __syncthreads();   // item scalars visible
+
+  // this warp's band of headdim rows
+  const int rpw = L.rpw;
+  const int r0 = min(warp * rpw, Pn), r1 = min(r0 + rpw, Pn);
+  const int nrow = r1 - r0;
+  const int hcol = lane % LPR;
+  const int nch = nrow * LPR;
+  const int ncb = nrow * CPR;
+  // FLUSH lane mapping: fcw chunk columns per pass, lane -> (row frr, column fcq)
+  const int fcw = nrow > 0 ? 32 / nrow : 1;
+  const int frr = nrow > 0 ? lane % nrow : 0;
+  const int fcq = nrow > 0 ? lane / nrow : 0;
+  const bool fok = nrow > 0 && fcq < fcw;
+  bool ok = true;
+
+  Cur q = start;
+  first_valid(q);
+  for (uint32_t k = 0; q.b * H + q.h < end; advance(q), ++k) {
+    const int j0b = q.b - b0, b = q.b, h = q.h, g = q.g;
+    const int slot = bslot[j0b], tnew = btn[j0b];
+    const int64_t sh = (int64_t)slot * H + h;
+    const int s = (int)(k % kStages);
+    const unsigned char* st = sm + s * L.stage_bytes;
+    if (!mbar_wait_bounded(&full[s], (k / kStages) & 1)) { ok = false; break; }
+    const uint4* csm = reinterpret_cast<const uint4*>(st + L.s_cold);
+    auto ring_x_at = [&](int j, int r) -> float {
+      return ring_st ? ldv<IOBF>(st + L.s_rx, j * Pn + r) : ldv<IOBF>(p.ring_x, (sh * c + j) * Pn + r);
+    };
+    auto ring_dt_at = [&](int j) -> float {
+      return ring_st ? reinterpret_cast<const float*>(st + L.s_rdt)[j] : p.ring_dt[sh * cp + j];
+    };
+    auto ring_b_at = [&](int j, int n) -> float {
+      return ring_st ? reinterpret_cast<const float*>(st + L.s_rb)[j * NC + n]
+                     : p.ring_b[(((int64_t)slot * p.G + g) * c + j) * NC + n];
+    };
+
+    if constexpr (STEP) {
+      const int it = b * H + h - beg;
+      const float* f = scal + it * kScal;
+      const float dt = f[0], dA = f[1], decay = f[2], eglog = f[3], glraw = f[4], Dh = f[5], A_h = f[6];
+      const int pcode = bpos[j0b];
+      const bool flush = pcode < 0;
+      const int pos = flush ? -pcode - 1 : pcode;
+      const unsigned char* xr = st + L.s_x;
+      const unsigned char* br = st + L.s_b;
+      const unsigned char* cr = st + L.s_c;
+
+      // ---- hot update of the band, written back to global; row sums of C.h
+      {
+        const float4* hs = reinterpret_cast<const float4*>(st + L.s_hot);
+        float4* hg = reinterpret_cast<float4*>(p.hot + sh * Pn * PB);
+        float bq[4], cq[4];
+        ld_row<4, IOBF>(br, hcol * 4, bq);
+        ld_row<4, IOBF>(cr, hcol * 4, cq);
+        const float2 dtB01 = f2(dt * bq[0], dt * bq[1]), dtB23 = f2(dt * bq[2], dt * bq[3]);
+        const float2 c01 = f2(cq[0], cq[1]), c23 = f2(cq[2], cq[3]);
+        const float2 dec2 = f2(decay, decay);
+#pragma unroll
+        for (int u = 0; u < HQ; ++u) {
+          if (u * 32 >= nch) break;   // uniform over the warp
+          const int lc = u * 32 + lane;
+          const int i = r0 * LPR + lc;
+          float part = 0.0f;
+          if (lc < nch) {
+            const float xp = ldv<IOBF>(xr, i / LPR);
+            const float2 x2 = f2(xp, xp);
+            const float4 v = hs[i];
+            const float2 a = __ffma2_rn(f2(v.x, v.y), dec2, __fmul2_rn(dtB01, x2));
+            const float2 bb = __ffma2_rn(f2(v.z, v.w), dec2, __fmul2_rn(dtB23, x2));
+            hg[i] = make_float4(a.x, a.y, bb.x, bb.y);
+            const float2 pr = __ffma2_rn(a, c01, __fmul2_rn(bb, c23));
+            part = pr.x + pr.y;
+          }
+#pragma unroll
+          for (int o = 1; o < LPR; o <<= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+          if (hcol == 0 && lc < nch) yh[i / LPR] = part;
+        }
+      }
+      // ---- stale cold readout of the band: per-chunk partials sum_e q[e] C[n]
+      if (p.mode != NSSM_MODE_COLDOFF) {
+#pragma unroll
+        for (int u = 0; u < CQ; ++u) {
+          if (u * 32 >= ncb) break;
+          const int lc = u * 32 + lane;
+          if (lc < ncb) {
+            const int i = r0 * CPR + lc;
+            const int cc = i % CPR;
+            float cv[CE];
+            ld_row<CE, IOBF>(cr, PB + cc * CE, cv);
+            const uint4 q4 = csm[i];
+            const uint32_t wv[4] = {q4.x, q4.y, q4.z, q4.w};
+            float2 acc = f2(0.0f, 0.0f);
+#pragma unroll
+            for (int wi = 0; wi < 4; ++wi) {
+              float qv[kPerW];
+              word_to_float<COLD>(wv[wi], qv);
+              if constexpr (kPerW >= 2) {
+#pragma unroll
+                for (int e = 0; e < kPerW; e += 2)
+                  acc = __ffma2_rn(f2(qv[e], qv[e + 1]), f2(cv[wi * kPerW + e], cv[wi * kPerW + e + 1]), acc);
+              } else {
+                acc.x = fmaf(qv[0], cv[wi], acc.x);
+              }
+            }
+            pc[i] = acc.x + acc.y;
+          }
+        }
+      }
+      // ---- exact rank-c correction weights (mode corr), per warp:
+      //      w_j = exp(G_t - G_j) (C_cold . B_j) for this chunk's tokens j <= t
+      const int J = pos + 1;
+      if (corr) {
+        if (lane == 0) {
+          float suf = 0.0f;
+          wsc[J - 1] = 1.0f;
+          wsc[c + J - 1] = dt;
+          for (int j = J - 2; j >= 0; --j) {
+            suf = suf + ((j + 1 == J - 1) ? dt : ring_dt_at(j + 1)) * A_h;
+            wsc[j] = expf(suf);
+            wsc[c + j] = ring_dt_at(j);
+          }
+        }
+        __syncwarp();
+        for (int j = 0; j < J; ++j) {
+          float sd = 0.0f;
+          for (int n = lane; n < NC; n += 32)
+            sd = fmaf(ldv<IOBF>(cr, PB + n), (j == J - 1) ? ldv<IOBF>(br, PB + n) : ring_b_at(j, n), sd);
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) sd += __shfl_xor_sync(0xffffffffu, sd, o);
+          __syncwarp();
+          if (lane == 0) wsc[j] = wsc[j] * sd;
+        }
+      }
+      __syncwarp();
+
+      // ---- y = C_hot.h + exp(glog) scale C_cold.cold (+ corr) + D x, one lane per row;
+      //      this token into the ring at pos
+      if (lane < nrow) {
+        const int row = r0 + lane;
+        const float xp = ldv<IOBF>(xr, row);
+        float y = yh[row];
+        if (p.mode != NSSM_MODE_COLDOFF) {
+          float yc = 0.0f;
+#pragma unroll
+          for (int cc = 0; cc < CPR; ++cc) yc += pc[row * CPR + cc];
+          const float scl = (COLD == COLD_FP8) ? reinterpret_cast<const float*>(st + L.s_scale)[row] : 1.0f;
+          y += (yc * scl) * eglog;
+        }
+        if (corr) {
+          float ycorr = 0.0f;
+          for (int j = 0; j < J; ++j) {
+            const float xj = (j == J - 1) ? xp : ring_x_at(j, row);
+            ycorr = fmaf(wsc[j], wsc[c + j] * xj, ycorr);
+          }
+          y += ycorr;
+        }
+        if (p.D) y = fmaf(xp, Dh, y);
+        st_io(p.out, (int64_t)b * p.out_sb + (int64_t)h * p.out_sh + row, p.out_dtype, y);
+        stv<IOBF>(p.ring_x, (sh * c + pos) * Pn + row, xp);
+      }
+      if (q.hr == 0) {   // the group's B_cold, once per group, spread over the warps
+        for (int n = tid; n < NC; n += kPT)
+          p.ring_b[(((int64_t)slot * p.G + g) * c + pos) * NC + n] = ldv<IOBF>(br, PB + n);
+      }
+      if (tid == 0) {
+        p.ring_dt[sh * cp + pos] = dt;
+        p.glog[sh] = flush ? 0.0f : glraw + dA;   // the FLUSH phase re-bases the cold slice
+        p.t[sh] = tnew;
+      }
+    } else {
+      // ---- FLUSH of the band: cold <- exp(sum dA) cold + sum_j exp(suf_j) (dt_j x_j) B_j,
+      // requantised; the ring holds all c tokens of the chunk.  Same operation order as
+      // the oracle: acc = sum_j (W_j * B_j[n]) in j order, mul then add;
+      // v = (q * scale) * exp(tot) + acc; fp8 scale = amax/448 + 1e-12 and
+      // q = rne(v / scale) with a correctly rounded division.
+      const float A_h = sA[h];
+      const bool pre = c <= kRingF32Max;
+      if (pre) {
+        const float* fs = reinterpret_cast<const float*>(sm + L.off_fsc) + (b * H + h - beg) * (2 * c + 1);
+        for (int e = lane; e < 2 * c + 1; e += 32) wsc[e] = fs[e];
+      } else if (lane == 0) {   // suffix decays (per warp; identical in every warp)
+        float tot = 0.0f;
+        for (int j = 0; j < c; ++j) tot = tot + ring_dt_at(j) * A_h;
+        wsc[2 * c] = expf(tot);
+        wsc[c - 1] = 1.0f;
+        wsc[c + c - 1] = ring_dt_at(c - 1);
+        float suf = 0.0f;
+        for (int j = c - 2; j >= 0; --j) {
+          suf = suf + ring_dt_at(j + 1) * A_h;
+          wsc[j] = expf(suf);
+          wsc[c + j] = ring_dt_at(j);
+        }
+      }
+      __syncwarp();
+      // W_j[row] = exp(suf_j) * (dt_j * x_j[row]) for the band's rows
+      for (int j = 0; j < c; ++j) {
+        if (lane < nrow) sW[j * Pn + r0 + lane] = __fmul_rn(wsc[j], __fmul_rn(wsc[c + j], ring_x_at(j, r0 + lane)));
+      }
+      __syncwarp();
+      const float etot = wsc[2 * c];
+      const float* scl_s = reinterpret_cast<const float*>(st + L.s_scale);
+      const float* rbp = ring_st ? reinterpret_cast<const float*>(st + L.s_rb)
+                                 : p.ring_b + ((int64_t)slot * p.G + g) * c * NC;
+      uint4* cst = reinterpret_cast<uint4*>(sm + s * L.stage_bytes + L.s_cold);   // requantised in place
+      // lane -> (row frr of the band, chunk column u*fcw + fcq): the 8 lanes of a
+      // shared-memory phase share a chunk column, so B_j reads are broadcasts
+      float v[CQF][CE];
+#pragma unroll
+      for (int u = 0; u < CQF; ++u) {
+        if (u * fcw >= CPR) break;   // uniform
+        const int cc0 = u * fcw + fcq;
+        const bool act = fok && cc0 < CPR;
+        const int cc = act ? cc0 : 0;
+        const int row = r0 + (fok ? frr : 0);
+        const int i = row * CPR + cc;
+#pragma unroll
+        for (int e = 0; e < CE; ++e) v[u][e] = 0.0f;
+#pragma unroll 4
+        for (int j = 0; j < c; ++j) {
+          const float Wv = sW[j * Pn + row];
+          const float2 W2 = f2(Wv, Wv);
+          const float4* b4 = reinterpret_cast<const float4*>(rbp + j * NC + cc * CE);
+#pragma unroll
+          for (int e = 0; e < CE / 4; ++e) {
+            const float4 bv = b4[e];
+            const float2 lo = __ffma2_rn(W2, f2(bv.x, bv.y), f2(v[u][4 * e], v[u][4 * e + 1]));
+            const float2 hi = __ffma2_rn(W2, f2(bv.z, bv.w), f2(v[u][4 * e + 2], v[u][4 * e + 3]));
+            v[u][4 * e] = lo.x; v[u][4 * e + 1] = lo.y; v[u][4 * e + 2] = hi.x; v[u][4 * e + 3] = hi.y;
+          }
+        }
+        const float scl = (COLD == COLD_FP8) ? scl_s[row] : 1.0f;
+        const uint4 q4 = csm[i];
+        const uint32_t wv[4] = {q4.x, q4.y, q4.z, q4.w};
+        const float2 e2 = f2(etot, etot), s2 = f2(scl, scl);
+        float m = 0.0f;
+#pragma unroll
+        for (int wi = 0; wi < 4; ++wi) {
+          float qv[kPerW];
+          word_to_float<COLD>(wv[wi], qv);
+          if constexpr (kPerW >= 2) {
+#pragma unroll
+            for (int e = 0; e < kPerW; e += 2) {
+              const int x = wi * kPerW + e;
+              float2 dq = f2(qv[e], qv[e + 1]);
+              if constexpr (COLD == COLD_FP8) dq = __fmul2_rn(dq, s2);
+              const float2 r2 = __fadd2_rn(__fmul2_rn(dq, e2), f2(v[u][x], v[u][x + 1]));
+              v[u][x] = r2.x;
+              v[u][x + 1] = r2.y;
+            }
+          } else {
+            v[u][wi] = __fadd_rn(__fmul_rn(qv[0], etot), v[u][wi]);
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < CE; ++e) m = fmaxf(m, fabsf(v[u][e]));
+        if (COLD == COLD_FP8 && act) pc[i] = m;
+      }
+      if constexpr (COLD == COLD_FP8) {
+        __syncwarp();
+        if (lane < nrow) {
+          const int row = r0 + lane;
+          float m = 0.0f;
+#pragma unroll
+          for (int cc = 0; cc < CPR; ++cc) m = fmaxf(m, pc[row * CPR + cc]);
+          const float sc = __fadd_rn(__fdiv_rn(m, kFp8Max), kScaleEps);
+          s_sc[row] = sc;
+          s_rcp[row] = __frcp_rn(sc);
+          p.scale[sh * Pn + row] = sc;
+        }
+        __syncwarp();
+      }
+#pragma unroll
+      for (int u = 0; u < CQF; ++u) {
+        if (u * fcw >= CPR) break;
+        const int cc0 = u * fcw + fcq;
+        if (fok && cc0 < CPR) {
+          const int row = r0 + frr;
+          if constexpr (COLD == COLD_FP8) {
+            // correctly rounded v / scale, two lanes at a time (Markstein's correction)
+            const float2 r2 = f2(s_rcp[row], s_rcp[row]);
+            const float2 nsc2 = f2(-s_sc[row], -s_sc[row]);
+#pragma unroll
+            for (int e = 0; e < CE; e += 2) {
+              const float2 a = f2(v[u][e], v[u][e + 1]);
+              const float2 q0 = __fmul2_rn(a, r2);
+              const float2 rs = __ffma2_rn(q0, nsc2, a);
+              const float2 qq = __ffma2_rn(rs, r2, q0);
+              v[u][e] = qq.x;
+              v[u][e + 1] = qq.y;
+            }
+          }
+          uint32_t wq[4];
+          float_to_cold<COLD, CE>(v[u], wq);
+          cst[row * CPR + cc0] = make_uint4(wq[0], wq[1], wq[2], wq[3]);
+        }
+      }
+      // the band's requantised rows -> global in one bulk store
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0 && nrow > 0) {
+        bulk_s2g(static_cast<char*>(p.cold) + (sh * Pn + r0) * NC * ESZ, cst + r0 * CPR,
+                 (uint32_t)(nrow * NC * ESZ));
+        bulk_commit();
+      }
+    }
+
+    // ---- release stage s (after this warp's bulk stores have read it); the producer
+    // refills it once every warp has
+    __syncwarp();
+    if (lane == 0) {
+      bulk_wait_read_all();
+      mbar_arrive(&empty[s]);
+    }
+    if (tid == 0 && pq.b * H + pq.h < end) {
+      if (!mbar_wait_bounded(&empty[s], (k / kStages) & 1)) { ok = false; break; }
+      fence_proxy_async_smem();
+      issue(pq, s);
+      ++n_issued;
+      advance(pq);
+    }
+  }
+  if (lane == 0) bulk_wait_all();   // this warp's bulk stores are complete before exit
+  if (!ok && tid == 0) {
+    // a wait timed out: flag it and keep the CTA (and its shared memory) alive until
+    // the copies it issued have landed (bounded again)
+    if (p.status) atomicOr(p.status, STATUS_TIMEOUT);
+    for (uint32_t qn = 0; qn < n_issued; ++qn) mbar_wait_bounded(&full[qn % kStages], (qn / kStages) & 1);
+  }
+}
+
+}  // namespace nssm

@@ -19,7 +19,7 @@ INCLUDE = os.path.join(REPO_DIR, "include")
 LIB_NAME = "libnested_ssm.so"
 LIB_PATH = os.path.join(PKG_DIR, LIB_NAME)
 
-SOURCES = ["nssm_abi.cu"]
+SOURCES = ["nssm_abi.cu", "nssm_pb16.cu", "nssm_pb32.cu", "nssm_pb64.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -52,21 +52,36 @@ def build(force: bool = False, ptxas_verbose: bool = False, quiet: bool = False,
     target = out or LIB_PATH
     if not force and out is None and not is_stale():
         return LIB_PATH
-    cmd = [nvcc_path(), *ARCH_FLAGS, "-lineinfo", "-O3", "-std=c++17", "--shared",
-           "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
-           "-I", INCLUDE, "-I", CSRC, "-o", target + ".tmp"]
+    common = [*ARCH_FLAGS, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC",
+              "-Xcompiler", "-fvisibility=hidden", "-I", INCLUDE, "-I", CSRC]
     for d in defines or []:
-        cmd.append("-D" + d)
+        common.append("-D" + d)
     if ptxas_verbose:
-        cmd += ["-Xptxas", "-v"]
-    cmd += [os.path.join(CSRC, s) for s in SOURCES]
-    if not quiet:
-        print("[nested_ssm_b200] " + " ".join(cmd), file=sys.stderr)
-    res = subprocess.run(cmd, capture_output=True, text=True)
+        common += ["-Xptxas", "-v"]
+    objdir = target + ".objs"
+    os.makedirs(objdir, exist_ok=True)
+    procs = []
+    for src in SOURCES:
+        obj = os.path.join(objdir, src.replace(".cu", ".o"))
+        cmd = [nvcc_path(), *common, "-c", os.path.join(CSRC, src), "-o", obj]
+        if not quiet:
+            print("[nested_ssm_b200] " + " ".join(cmd), file=sys.stderr)
+        procs.append((obj, subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)))
+    objs, errs = [], []
+    for obj, pr in procs:
+        out, err = pr.communicate()
+        if pr.returncode != 0:
+            errs.append(f"{obj}: nvcc failed ({pr.returncode}):\n{out}\n{err}")
+        elif ptxas_verbose:
+            print(err, file=sys.stderr)
+        objs.append(obj)
+    if errs:
+        raise RuntimeError("\n".join(errs))
+    link = [nvcc_path(), *ARCH_FLAGS, "--shared", "-o", target + ".tmp", *objs]
+    res = subprocess.run(link, capture_output=True, text=True)
     if res.returncode != 0:
-        raise RuntimeError(f"nvcc failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
-    if ptxas_verbose:
-        print(res.stderr, file=sys.stderr)
+        raise RuntimeError(f"nvcc link failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
+    shutil.rmtree(objdir, ignore_errors=True)
     os.replace(target + ".tmp", target)
     return target
 

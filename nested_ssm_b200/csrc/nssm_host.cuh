@@ -1,0 +1,198 @@
+// Host-side launch helpers shared by the translation units of libnested_ssm:
+// validation results are reported through fail() (thread-local message), and each
+// (dstate, hot width, cold dtype, io dtype) instance is launched by the templates
+// below.  nssm_pb16/32/64.cu instantiate them per hot width (compiled in parallel);
+// nssm_abi.cu holds the extern "C" entry points.
+#pragma once
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "nssm_persistent.cuh"
+
+namespace nssm_host {
+
+int fail(int code, const char* fmt, ...);
+int cuda_check(const char* what);
+int occupancy(const void* fn, int smem, int threads, int* occ_out);
+int sm_count(int* out);
+int smem_optin(int* out);
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+inline int io_bytes(int dt) { return dt == NSSM_BF16 ? 2 : 4; }
+
+inline int round_up(int v, int m) { return (v + m - 1) / m * m; }
+
+using nssm::COLD_BF16;
+using nssm::COLD_F32;
+using nssm::COLD_FP8;
+using nssm::COLD_NONE;
+
+constexpr int kTPR = 2;        // threads per headdim row, tiered kernels
+constexpr int kTPRFresh = 4;   // threads per headdim row, untiered kernel
+
+template <int PB, int NC, int COLD>
+size_t step_smem_bytes(int P, int c) {
+  return sizeof(float) * nssm::StepShape<PB, NC, COLD>::smem_floats(P, c);
+}
+
+// ---- launchers ------------------------------------------------------------
+template <int PB, int NC, int COLD, int TPR>
+int launch_step(const nssm::StepParams& sp, int batch, cudaStream_t st) {
+  dim3 grid(sp.H, batch);
+  const int threads = round_up(sp.P * TPR, 32);
+  nssm::tiered_step_kernel<PB, NC, COLD, TPR><<<grid, threads, step_smem_bytes<PB, NC, COLD>(sp.P, sp.c), st>>>(sp);
+  return cuda_check("tiered_step_kernel launch");
+}
+
+// The persistent TMA-pipelined kernels move every per-item operand with 1-D bulk
+// copies, so they need 16-byte aligned rows: headdim % 4 == 0 and <= 80, x / B / C
+// bases and strides 16-byte aligned.  Anything else runs the simple kernel.
+template <int PB, int NC, int COLD, bool IOBF, int PHASE, int CFIX, int RPWC>
+inline int launch_phase(const nssm::StepParams& sp, int batch, cudaStream_t st, bool ring_ok, int sms, bool* done) {
+  *done = false;
+  const long long items = (long long)batch * sp.H;
+  auto fn = nssm::tiered_persistent_kernel<PB, NC, COLD, IOBF, PHASE, CFIX, RPWC>;
+  const int iob = IOBF ? 2 : 4;
+  const int minb = PHASE == nssm::PH_STEP ? NSSM_STEP_P_MINB : NSSM_FLUSH_P_MINB;
+  int optin = 0;
+  int rc = smem_optin(&optin);
+  if (rc) return rc;
+  for (int target = minb; target >= 1; --target) {
+    long long grid = (long long)sms * target;
+    if (grid > items) grid = items;
+    const long long per_cta = (items + grid - 1) / grid;
+    const int maxb = (int)((per_cta + sp.H - 1) / sp.H) + 2;
+    nssm::PParams pp{};
+    pp.sp = sp;
+    pp.items = (int)items;
+    pp.ring_in_stage = ring_ok ? 1 : 0;
+    // deepest pipeline (up to the phase's stage count) whose CTAs fit `target` per SM
+    int nst = nssm::stages_for(PHASE);
+    for (; nst >= 2; --nst) {
+      pp.L = nssm::make_playout<PB, NC, COLD>(PHASE, sp.mode == NSSM_MODE_CORR, sp.P, sp.H, sp.c, iob, maxb,
+                                              (int)per_cta, ring_ok, nst);
+      if (pp.L.total <= optin && (long long)target * (pp.L.total + 1024) <= 228 * 1024) break;
+    }
+    if (nst < 2) continue;
+    int occ = 0;
+    rc = occupancy(reinterpret_cast<const void*>(fn), pp.L.total, nssm::kPT, &occ);
+    if (rc) return rc;
+    if (occ >= target) {
+      fn<<<(unsigned)grid, nssm::kPT, pp.L.total, st>>>(pp);
+      *done = true;
+      return cuda_check("tiered_persistent_kernel launch");
+    }
+  }
+  return NSSM_OK;
+}
+
+// Both phases of one step.  The production configuration (fp8 cold, bf16 io) has
+// instances compiled for c in {4, 8, 16} and headdim in {64, 80}; anything else
+// runs the instances that read c and headdim at run time.
+template <int PB, int NC, int COLD, bool IOBF, int CFIX, int RPWC>
+inline int launch_both(const nssm::StepParams& sp, int batch, cudaStream_t st, bool ring_ok, int sms) {
+  bool done = false;
+  int rc = launch_phase<PB, NC, COLD, IOBF, nssm::PH_STEP, CFIX, RPWC>(sp, batch, st, ring_ok, sms, &done);
+  if (rc) return rc;
+  if (!done) return launch_step<PB, NC, COLD, kTPR>(sp, batch, st);
+  rc = launch_phase<PB, NC, COLD, IOBF, nssm::PH_FLUSH, CFIX, RPWC>(sp, batch, st, ring_ok, sms, &done);
+  if (rc) return rc;
+  if (!done) return fail(NSSM_ERR_UNSUPPORTED, "flush phase does not fit this device");
+  return NSSM_OK;
+}
+
+template <int PB, int NC, int COLD, bool IOBF, int RPWC>
+inline int launch_c(const nssm::StepParams& sp, int batch, cudaStream_t st, bool ring_ok, int sms) {
+  switch (sp.c) {
+    case 4: return launch_both<PB, NC, COLD, IOBF, 4, RPWC>(sp, batch, st, ring_ok, sms);
+    case 8: return launch_both<PB, NC, COLD, IOBF, 8, RPWC>(sp, batch, st, ring_ok, sms);
+    case 16: return launch_both<PB, NC, COLD, IOBF, 16, RPWC>(sp, batch, st, ring_ok, sms);
+  }
+  return launch_both<PB, NC, COLD, IOBF, 0, 0>(sp, batch, st, ring_ok, sms);
+}
+
+template <int PB, int NC, int COLD, bool IOBF>
+inline int launch_persistent(const nssm::StepParams& sp, int batch, cudaStream_t st, bool ring_ok) {
+  const long long items = (long long)batch * sp.H;
+  if (items > (1ll << 30)) return launch_step<PB, NC, COLD, kTPR>(sp, batch, st);
+  int sms = 0;
+  int rc = sm_count(&sms);
+  if (rc) return rc;
+  if constexpr (COLD == nssm::COLD_FP8 && IOBF) {
+    if (sp.P == 80) return launch_c<PB, NC, COLD, IOBF, 10>(sp, batch, st, ring_ok, sms);
+    if (sp.P == 64) return launch_c<PB, NC, COLD, IOBF, 8>(sp, batch, st, ring_ok, sms);
+  }
+  return launch_both<PB, NC, COLD, IOBF, 0, 0>(sp, batch, st, ring_ok, sms);
+}
+
+template <int PB, int NC, int COLD>
+inline int launch_tiered(const nssm::StepParams& sp, int batch, cudaStream_t st) {
+  constexpr int N = PB + NC;
+  const int iob = io_bytes(sp.io_dtype);
+#ifdef NSSM_FORCE_SIMPLE
+  return launch_step<PB, NC, COLD, kTPR>(sp, batch, st);
+#endif
+  auto a16 = [](long long v) { return (v % 16) == 0; };
+  const bool tma_ok = sp.P % 4 == 0 && sp.P <= nssm::kPMaxPersistent && aligned16(sp.hot) &&
+                      aligned16(sp.cold) && (COLD != COLD_FP8 || aligned16(sp.scale)) && aligned16(sp.x) &&
+                      a16(sp.x_sb * iob) && a16(sp.x_sh * iob) && a16((long long)sp.P * iob) &&
+                      aligned16(sp.B) && aligned16(sp.C) && a16(sp.B_sb * iob) && a16(sp.C_sb * iob) &&
+                      a16((long long)N * iob);
+  if (!tma_ok) return launch_step<PB, NC, COLD, kTPR>(sp, batch, st);
+  const bool ring_ok = sp.c <= nssm::kRingInStage && aligned16(sp.ring_x) && aligned16(sp.ring_b) &&
+                       aligned16(sp.ring_dt) && a16((long long)sp.c * sp.P * iob) &&
+                       a16((long long)sp.c * NC * 4);
+  if (sp.io_dtype == NSSM_BF16) return launch_persistent<PB, NC, COLD, true>(sp, batch, st, ring_ok);
+  return launch_persistent<PB, NC, COLD, false>(sp, batch, st, ring_ok);
+}
+
+template <int PB, int NC, int COLD, int TPR>
+int launch_split(const nssm::SplitParams& sp, int batch, cudaStream_t st) {
+  dim3 grid(sp.H, batch);
+  const int threads = round_up(sp.P * TPR, 32);
+  nssm::prefill_split_kernel<PB, NC, COLD, TPR><<<grid, threads, 0, st>>>(sp);
+  return cuda_check("prefill_split_kernel launch");
+}
+
+template <int PB, int NC, int COLD, int TPR>
+int launch_mat(const nssm::MatParams& mp, int batch, cudaStream_t st) {
+  dim3 grid(mp.H, batch);
+  const int threads = round_up(mp.P * TPR, 32);
+  nssm::materialize_kernel<PB, NC, COLD, TPR><<<grid, threads, 2 * nssm::kMaxChunk * sizeof(float), st>>>(mp);
+  return cuda_check("materialize_kernel launch");
+}
+
+// Instances compiled: dstate 128, hot width 16/32/64, cold fp8/bf16/fp32.
+enum Op { OP_STEP, OP_SPLIT, OP_MAT };
+
+template <int PB, int COLD>
+int run_op(Op op, const void* params, int batch, cudaStream_t st) {
+  constexpr int NC = 128 - PB;
+  switch (op) {
+    case OP_STEP: return launch_tiered<PB, NC, COLD>(*static_cast<const nssm::StepParams*>(params), batch, st);
+    case OP_SPLIT: return launch_split<PB, NC, COLD, kTPR>(*static_cast<const nssm::SplitParams*>(params), batch, st);
+    case OP_MAT: return launch_mat<PB, NC, COLD, kTPR>(*static_cast<const nssm::MatParams*>(params), batch, st);
+  }
+  return fail(NSSM_ERR_INVALID, "unknown op");
+}
+
+template <int PB>
+int run_cold(Op op, int cold, const void* params, int batch, cudaStream_t st) {
+  switch (cold) {
+    case NSSM_F8E4M3: return run_op<PB, COLD_FP8>(op, params, batch, st);
+    case NSSM_BF16: return run_op<PB, COLD_BF16>(op, params, batch, st);
+    case NSSM_F32: return run_op<PB, COLD_F32>(op, params, batch, st);
+  }
+  return fail(NSSM_ERR_INVALID, "cold_dtype %d is not one of F32/BF16/F8E4M3", cold);
+}
+
+int dispatch_pb16(Op op, int cold, const void* params, int batch, cudaStream_t st);
+int dispatch_pb32(Op op, int cold, const void* params, int batch, cudaStream_t st);
+int dispatch_pb64(Op op, int cold, const void* params, int batch, cudaStream_t st);
+
+}  // namespace nssm_host

@@ -1,0 +1,10 @@
+// Tiered-step / prefill-split / materialise instances for hot width 32.
+#include "nssm_host.cuh"
+
+namespace nssm_host {
+
+int dispatch_pb32(Op op, int cold, const void* params, int batch, cudaStream_t st) {
+  return run_cold<32>(op, cold, params, batch, st);
+}
+
+}  // namespace nssm_host

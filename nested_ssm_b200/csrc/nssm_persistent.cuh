@@ -125,6 +125,7 @@ struct PLayout {
   int off_scal, off_head, off_yh, off_pc, off_sc, off_rcp, off_wsc, off_sw, off_rbw, off_fsc, off_bslot, off_bmeta,
       off_bpos, off_bar;
   int total;
+  int nst;          // pipeline stages
   int rpw;          // headdim rows per warp band
   int wsc_stride;   // floats of per-warp scratch (suffix decays / corr weights)
   int maxb;         // batch rows one CTA can touch
@@ -137,7 +138,7 @@ constexpr int kScal = 8;   // per-item scalars (STEP): dt, dA, exp(dA), exp(glog
 
 template <int PB, int NC, int COLD>
 __host__ inline PLayout make_playout(int phase, bool corr, int P, int H, int c, int io_bytes, int maxb,
-                                     int maxitems, bool ring_in_stage) {
+                                     int maxitems, bool ring_in_stage, int nst) {
   constexpr int N = PB + NC;
   constexpr int ESZ = ColdTraits<COLD>::kBytes;
   constexpr int CPR = (NC * ESZ) / 16;
@@ -157,7 +158,7 @@ __host__ inline PLayout make_playout(int phase, bool corr, int P, int H, int c, 
   L.stage_bytes = al(o, 128);
   L.rpw = (P + kPW - 1) / kPW;
   L.wsc_stride = al(2 * c + 2, 4);
-  const int nst = stages_for(phase);
+  L.nst = nst;
   int t = nst * L.stage_bytes;
   L.off_scal = t; t += (step ? maxitems * kScal * 4 : 0);
   L.off_head = t; t += H * 4;                    // A per head (FLUSH)
@@ -246,9 +247,10 @@ __device__ __forceinline__ void ld_row(const unsigned char* row, int n0, float* 
   }
 }
 
-// CFIX > 0 compiles the kernel for that flush period (unrolled replay loops);
-// 0 takes c from the parameters.
-template <int PB, int NC, int COLD, bool IOBF, int PHASE, int CFIX>
+// CFIX > 0 compiles the kernel for that flush period (unrolled replay loops) and
+// RPWC > 0 for headdim == 8 * RPWC (every warp band RPWC rows); 0 takes them from
+// the parameters.
+template <int PB, int NC, int COLD, bool IOBF, int PHASE, int CFIX, int RPWC>
 __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSSM_FLUSH_P_MINB)
     tiered_persistent_kernel(const __grid_constant__ PParams pp) {
   using Sh = StepShape<PB, NC, COLD>;
@@ -260,8 +262,7 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
   constexpr int kPerW = WordTraits<COLD>::kPer;
   constexpr int IOB = IOBF ? 2 : 4;
   constexpr bool STEP = PHASE == PH_STEP;
-  constexpr int kStages = stages_for(PHASE);
-  constexpr int RPWMAX = (kPMaxPersistent + kPW - 1) / kPW;   // rows per warp band
+  constexpr int RPWMAX = RPWC > 0 ? RPWC : (kPMaxPersistent + kPW - 1) / kPW;   // rows per warp band
   constexpr int HQ = (RPWMAX * LPR + 31) / 32;                // hot chunks per lane
   constexpr int CQ = (RPWMAX * CPR + 31) / 32;                // cold chunks per lane (STEP)
   constexpr int CQF = (CPR + (32 / RPWMAX) - 1) / (32 / RPWMAX);   // column passes (FLUSH)
@@ -271,6 +272,7 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
 
   const StepParams& p = pp.sp;
   const PLayout& L = pp.L;
+  const int kStages = L.nst;
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int c = CFIX > 0 ? CFIX : p.c;
@@ -283,7 +285,7 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
 
   extern __shared__ __align__(128) unsigned char sm[];
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + L.off_bar);
-  uint64_t* empty = full + kStages;
+  uint64_t* empty = full + L.nst;
   const float* scal = reinterpret_cast<const float*>(sm + L.off_scal);
   float* sA = reinterpret_cast<float*>(sm + L.off_head);
   float* yh = reinterpret_cast<float*>(sm + L.off_yh);
@@ -453,10 +455,10 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
   }
   __syncthreads();   // item scalars visible
 
-  // this warp's band of headdim rows
-  const int rpw = L.rpw;
-  const int r0 = min(warp * rpw, Pn), r1 = min(r0 + rpw, Pn);
-  const int nrow = r1 - r0;
+  // this warp's band of headdim rows (compile-time when RPWC > 0: headdim == kPW * RPWC)
+  const int rpw = RPWC > 0 ? RPWC : L.rpw;
+  const int r0 = RPWC > 0 ? warp * RPWC : min(warp * rpw, Pn);
+  const int nrow = RPWC > 0 ? RPWC : min(r0 + rpw, Pn) - r0;
   const int hcol = lane % LPR;
   const int nch = nrow * LPR;
   const int ncb = nrow * CPR;
@@ -469,13 +471,14 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
 
   Cur q = start;
   first_valid(q);
+  int s = 0;
+  uint32_t par = 0;   // stage s / its phase parity for item k
   for (uint32_t k = 0; q.b * H + q.h < end; advance(q), ++k) {
     const int j0b = q.b - b0, b = q.b, h = q.h, g = q.g;
     const int slot = bslot[j0b], tnew = btn[j0b];
     const int64_t sh = (int64_t)slot * H + h;
-    const int s = (int)(k % kStages);
     const unsigned char* st = sm + s * L.stage_bytes;
-    if (!mbar_wait_bounded(&full[s], (k / kStages) & 1)) { ok = false; break; }
+    if (!mbar_wait_bounded(&full[s], par)) { ok = false; break; }
     const uint4* csm = reinterpret_cast<const uint4*>(st + L.s_cold);
     auto ring_x_at = [&](int j, int r) -> float {
       return ring_st ? ldv<IOBF>(st + L.s_rx, j * Pn + r) : ldv<IOBF>(p.ring_x, (sh * c + j) * Pn + r);
@@ -766,19 +769,25 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
       mbar_arrive(&empty[s]);
     }
     if (tid == 0 && pq.b * H + pq.h < end) {
-      if (!mbar_wait_bounded(&empty[s], (k / kStages) & 1)) { ok = false; break; }
+      if (!mbar_wait_bounded(&empty[s], par)) { ok = false; break; }
       fence_proxy_async_smem();
       issue(pq, s);
       ++n_issued;
       advance(pq);
     }
+    if (++s == kStages) { s = 0; par ^= 1u; }
   }
   if (lane == 0) bulk_wait_all();   // this warp's bulk stores are complete before exit
   if (!ok && tid == 0) {
     // a wait timed out: flag it and keep the CTA (and its shared memory) alive until
     // the copies it issued have landed (bounded again)
     if (p.status) atomicOr(p.status, STATUS_TIMEOUT);
-    for (uint32_t qn = 0; qn < n_issued; ++qn) mbar_wait_bounded(&full[qn % kStages], (qn / kStages) & 1);
+    int sq = 0;
+    uint32_t pq2 = 0;
+    for (uint32_t qn = 0; qn < n_issued; ++qn) {
+      mbar_wait_bounded(&full[sq], pq2);
+      if (++sq == kStages) { sq = 0; pq2 ^= 1u; }
+    }
   }
 }
 

@@ -113,6 +113,38 @@ def cold_values_close(gpool, opool, layer=0, slots=None, cold_kind="fp8", max_co
     return frac
 
 
+def cold_error_budget(gpool, opool, budget=None, layer=0, slots=None, cold_kind="fp8", max_code_frac=1e-3):
+    """Free-running bound on the stored cold state, for a run whose GPU and oracle
+    states are never re-synchronised.  The cold recurrence is contractive
+    (v <- v * exp(sum dt*A) + update, exp(...) <= 1, the update computed from the same
+    inputs on both sides), so an error made by one requantisation is carried but
+    never amplified; what can build up is at most one storage ulp per requantisation.
+    ``budget`` accumulates that ulp (relative ulp of the value now, or 0.2% of the row
+    amax near zero) step by step; every value must stay within it.  Returns the new
+    budget for the next call."""
+    sl = slots if slots is not None else torch.arange(opool.num_slots)
+    sl = sl[sl >= 0].long()
+    gq, oq = gpool.cold[layer].cpu()[sl], opool.cold[sl]
+    if cold_kind == "fp8":
+        gv = O.dequantize_rows(gq, gpool.scale[layer].cpu()[sl])
+        ov = O.dequantize_rows(oq, opool.scale[sl])
+        d = fp8_ulp_dist(gq, oq)
+        rel = 0.13
+    else:
+        gv, ov = gq.float(), oq.float()
+        d = bf16_ulp_dist(gq, oq)
+        rel = 2.0 ** -7
+    amax = ov.abs().amax(dim=-1, keepdim=True)
+    per = rel * ov.abs() + 2e-3 * amax + 1e-7
+    budget = per if budget is None else budget + per
+    err = (gv - ov).abs()
+    worst = float((err / budget).max())
+    assert worst <= 1.0, f"{cold_kind} cold value off by {worst:.2f}x the accumulated one-ulp-per-step budget"
+    frac = float((d > 0).float().mean())
+    assert frac <= max_code_frac, f"{cold_kind}: {frac:.2e} of codes differ"
+    return budget
+
+
 def assert_y_close_quantized(y_gpu, y_ref, what=""):
     """y of a free-running run with quantised cold: a one-ulp cold code flip moves
     y by C[n]*ulp, so allow rare (<0.1%) excursions up to 1e-2 beyond the y bar."""

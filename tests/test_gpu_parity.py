@@ -67,14 +67,16 @@ def test_per_step_parity_from_identical_state(cold, pb, c):
 def test_free_running_matches_oracle(cold, pb, c):
     """Free-running for several flushes.  fp32 cold: the strict bar throughout.
     fp8 / bf16 cold: a code that flips once (exp / log1p differ by an ulp between
-    the GPU and the CPU) is carried and compounded through later flushes, so the
-    bound is in value terms (three storage ulps, or 0.6% of the row amax) and y may
-    move by a flipped code's C[n] * ulp.  The one-ulp bar is the per-step test."""
+    the GPU and the CPU) is carried through later flushes (never amplified: the cold
+    recurrence is contractive), so the state bound is one storage ulp per step,
+    accumulated, and y may move by a flipped code's C[n] * ulp.  The one-ulp bar is
+    the per-step test."""
     steps = 2 * c + 3
     case = Hh.make_case(b=6, S=10, pb=pb, c=c, cold=cold, steps=steps, seed=pb + c)
     opool, gpool = Hh.oracle_pool(case), Hh.gpu_pool(case)
     slots = torch.tensor([7, 2, 9, 0, 4, 5])
     _split_both(case, gpool, opool, slots)
+    budget = None
     for s in range(steps):
         yg, yo = Hh.step_both(case, gpool, opool, s, slots)
         if cold == "fp32":
@@ -83,7 +85,7 @@ def test_free_running_matches_oracle(cold, pb, c):
         else:
             Hh.assert_y_close_quantized(yg, yo, f"step {s}")
             torch.testing.assert_close(gpool.hot[0].cpu()[slots], opool.hot[slots], rtol=1e-5, atol=1e-6)
-            Hh.cold_values_close(gpool, opool, 0, slots, cold, ulps=3)
+            budget = Hh.cold_error_budget(gpool, opool, budget, 0, slots, cold)
 
 
 def test_large_batch_pipeline_wraps():

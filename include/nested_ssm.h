@@ -142,6 +142,27 @@ NSSM_API size_t nssm_step_workspace_bytes(int32_t batch, int32_t ngroups, int32_
  * writes y = C_hot.h_hot + exp(glog) C_cold.cold + D x to out. */
 NSSM_API int nssm_tiered_step(const nssm_pool* pool, const nssm_step_args* args, void* stream);
 
+/* Bytes of the library's static rotation scratch (one copy per device). */
+#define NSSM_STATIC_SCRATCH_BYTES (4u << 20)
+
+/* nssm_tiered_step without a caller workspace: for hosts that cannot allocate
+ * device memory on the library's behalf (a server whose memory planner owns
+ * every allocation, or an FFI binding that passes only the model's tensors).
+ * No counterpart in the reference, which always allocates through torch.
+ *  - args->workspace / workspace_bytes are ignored; the rotated B and C go to
+ *    a fixed NSSM_STATIC_SCRATCH_BYTES array in the library's own device
+ *    memory.  Nothing is allocated and nothing has to start at zero.
+ *  - Limit: nssm_step_workspace_bytes(batch, ngroups, dstate, io_dtype, 1)
+ *    must not exceed NSSM_STATIC_SCRATCH_BYTES (batch <= 1024 for bf16 and
+ *    <= 512 for f32 at ngroups 8, dstate 128); larger calls return
+ *    NSSM_ERR_INVALID.  Without R no scratch is used and there is no limit.
+ *  - The first call on each device looks the array up (a one-time set-up, on
+ *    the current device); make that call before any stream capture begins.
+ *  - All calls on one device share the array: two calls with R that may run
+ *    at the same time (different streams, or different host threads) race and
+ *    corrupt each other's B and C.  Issue them on one stream. */
+NSSM_API int nssm_tiered_step_static(const nssm_pool* pool, const nssm_step_args* args, void* stream);
+
 /* Untiered fp32 update of a full state [num_slots][nheads][headdim][dstate]
  * (replaces selective_state_update; the fresh control). */
 NSSM_API int nssm_fresh_step(float* state, int32_t num_slots, int32_t nheads, int32_t headdim,

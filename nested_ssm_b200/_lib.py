@@ -20,7 +20,7 @@ ABI_VERSION = 1
 EXPORTED = (
     "nssm_step_workspace_bytes", "nssm_tiered_step", "nssm_fresh_step", "nssm_prefill_split",
     "nssm_materialize", "nssm_rot_flat", "nssm_supported_hot_dims", "nssm_sizeof_pool",
-    "nssm_sizeof_step_args", "nssm_abi_version", "nssm_last_error",
+    "nssm_sizeof_step_args", "nssm_abi_version", "nssm_last_error", "nssm_tiered_step_static",
 )
 
 
@@ -88,6 +88,7 @@ def load(auto_build: bool = True) -> C.CDLL:
         sig = {
             "nssm_step_workspace_bytes": (sz, [i32, i32, i32, i32, i32]),
             "nssm_tiered_step": (C.c_int, [P_pool, P_args, vp]),
+            "nssm_tiered_step_static": (C.c_int, [P_pool, P_args, vp]),
             "nssm_fresh_step": (C.c_int, [vp, i32, i32, i32, i32, i32, P_args, vp]),
             "nssm_prefill_split": (C.c_int, [P_pool, vp, i64, vp, i32, i32, vp]),
             "nssm_materialize": (C.c_int, [P_pool, vp, vp, i32, i32, vp, i64, vp]),

@@ -1,0 +1,210 @@
+"""Generate the golden fixtures of tests/golden/ by running the REFERENCE's own Python
+on the CPU (the fixtures are committed; this script is how they were made).
+
+    python tests/golden/make_golden.py --reference <checkout of omin-Kwon/nested_ssm>
+
+Three fixtures, all from seeded inputs that ``oracle.make_params`` / ``oracle.make_inputs``
+regenerate (checksums stored beside the outputs):
+
+* ``native_decode_fp32.npz`` -- ``_v4_decode`` of ``scale/v4_native_decode.py:26-172``
+  (the HF NemotronH decode branch with the tiered readout), fp32 hot and cold, pb=32, c=4,
+  modes stale / corr / coldoff.  It is driven through a stub mixer whose in_proj, act,
+  norm and out_proj are identities and whose conv1d passes the newest column through,
+  so its inputs are exactly the (x, rotated B, rotated C, dt_raw) the state op sees and
+  its output is the pre-norm y.  Rotation: ``rot_flat`` of ``scale/vllm_v4_patch.py:41-45``
+  called on fp32 B, C (the fp32 einsum of ``scale/v4_fused_decode.py:47-48``), cast to bf16.
+* ``vllm_fp8.npz`` -- ``prefill_snapshot`` / ``decode_readout`` of
+  ``scale/vllm_v4_patch.py:123-179`` with fp8 cold snapshots on a stub mixer; the fresh
+  state update that vLLM's selective_state_update performs before the readout is done
+  here in torch (softplus without clamp, as vLLM).
+* ``rot_flat.npz`` -- ``rot_flat`` on bf16 input (the bf16 einsum of ActRotMask) and on
+  fp32 input.
+"""
+from __future__ import annotations
+
+import argparse
+import math
+import os
+import sys
+import types
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, REPO)
+
+import oracle as O  # noqa: E402
+
+# fixture shapes (small enough to commit, real headdim / d_state / hot width)
+NATIVE = dict(b=2, H=16, P=80, N=128, G=2, pb=32, c=4, seed=11, steps=13, steps_modes=9)
+VLLM = dict(b=2, S=4, H=8, P=80, N=128, G=2, pb=32, c=4, seed=12, steps=9, slots=[2, 0])
+ROT = dict(T=6, G=2, N=128, seed=13)
+
+
+def state0(b, H, P, N, seed):
+    g = torch.Generator().manual_seed(seed + 7)
+    return torch.randn(b, H, P, N, generator=g) * math.sqrt(0.1)
+
+
+def checksum(t: torch.Tensor) -> float:
+    return float(t.double().sum())
+
+
+def _conv_cache(conv_dim, K=4):
+    """Stub cache: update_conv_state returns the new column at the newest tap only."""
+    cache = types.SimpleNamespace()
+
+    def update_conv_state(hs, idx):          # hs [b, conv_dim, 1]
+        b = hs.shape[0]
+        st = torch.zeros(b, conv_dim, K, dtype=hs.dtype)
+        st[..., -1] = hs[..., -1]
+        return st
+
+    def update_recurrent_state(s, idx):
+        cache.layers[idx].recurrent_states = s
+        return s
+
+    cache.update_conv_state = update_conv_state
+    cache.update_recurrent_state = update_recurrent_state
+    return cache
+
+
+def run_native(V, rot_flat, cfg, mode):
+    b, H, P, N, G, pb, c, seed = (cfg[k] for k in ("b", "H", "P", "N", "G", "pb", "c", "seed"))
+    steps = cfg["steps"] if mode == "stale" else cfg["steps_modes"]
+    prm = O.make_params(H, G, N, seed=seed)[0]
+    xs, dts, Bs, Cs = O.make_inputs(b, H, P, G, N, steps, seed=seed, io_dtype=torch.bfloat16)
+    s0 = state0(b, H, P, N, seed)
+    A_log = torch.log(-prm["A"])
+    A = -torch.exp(A_log.float())                       # what the mixer computes
+    K = 4
+    I, conv_dim = H * P, H * P + 2 * G * N
+    m = types.SimpleNamespace(
+        num_heads=H, head_dim=P, ssm_state_size=N, n_groups=G, intermediate_size=I,
+        conv_dim=conv_dim, in_proj=torch.nn.Identity(), act=torch.nn.Identity(),
+        use_conv_bias=False, A_log=A_log, D=prm["D"], dt_bias=prm["dt_bias"],
+        time_step_min=1e-3, layer_idx=0, out_proj=torch.nn.Identity(),
+        norm=lambda y, gate: y,
+        v4cfg=dict(pb=pb, c=c, cold_bf16=0, corr=int(mode == "corr"), coldoff=int(mode == "coldoff")))
+    w = torch.zeros(conv_dim, 1, K)
+    w[:, 0, -1] = 1.0
+    m.conv1d = types.SimpleNamespace(weight=w, bias=torch.zeros(conv_dim))
+    m._v4state = {"snap": s0[..., pb:].clone(), "glog": torch.zeros(b, H, P), "t": 0,
+                  "bufB": [], "bufX": [], "bufG": []}
+    cache = _conv_cache(conv_dim, K)
+    cache.layers = [types.SimpleNamespace(recurrent_states=s0.clone())]
+    ys, Brs, Crs = [], [], []
+    for s in range(steps):
+        Br = rot_flat(Bs[s].reshape(b, G * N).float(), prm["R"]).to(torch.bfloat16)
+        Cr = rot_flat(Cs[s].reshape(b, G * N).float(), prm["R"]).to(torch.bfloat16)
+        Brs.append(Br.reshape(b, G, N))
+        Crs.append(Cr.reshape(b, G, N))
+        gate = torch.zeros(b, I)
+        proj = torch.cat([gate, xs[s].float().reshape(b, I), Br.float(), Cr.float(),
+                          dts[s].float()], dim=-1)[:, None, :]
+        y = V._v4_decode(m, proj, cache, None)
+        ys.append(y.reshape(b, H, P).float())
+    out = dict(y=torch.stack(ys), Br=torch.stack(Brs), Cr=torch.stack(Crs))   # B', C' bf16 (stored as int16 bits)
+    if mode == "stale":
+        out["state_final_h0_h9"] = cache.layers[0].recurrent_states[:, [0, 9]].float()
+    out["t_final"] = torch.tensor(m._v4state["t"])
+    meta = dict(x=checksum(xs), dt=checksum(dts), B=checksum(Bs), C=checksum(Cs), s0=checksum(s0))
+    return out, prm, A, meta
+
+
+def make_native(ref):
+    sys.path.insert(0, os.path.join(ref, "scale"))
+    import v4_native_decode as V
+    import vllm_v4_patch as VP
+    arrays = {}
+    for mode in ("stale", "corr", "coldoff"):
+        out, prm, A, meta = run_native(V, VP.rot_flat, NATIVE, mode)
+        for k, v in out.items():
+            arrays[f"{mode}_{k}"] = v
+        for k, v in meta.items():
+            arrays[f"{mode}_sum_{k}"] = torch.tensor(v, dtype=torch.float64)
+    arrays["R"] = prm["R"]
+    arrays["A"] = A
+    arrays["D"] = prm["D"]
+    arrays["dt_bias"] = prm["dt_bias"]
+    return arrays
+
+
+def make_vllm(ref):
+    sys.path.insert(0, os.path.join(ref, "scale"))
+    import vllm_v4_patch as VP
+    cfg = VLLM
+    b, S, H, P, N, G, pb, c, seed = (cfg[k] for k in ("b", "S", "H", "P", "N", "G", "pb", "c", "seed"))
+    steps = cfg["steps"]
+    slots = torch.tensor(cfg["slots"])
+    prm = O.make_params(H, G, N, seed=seed)[0]
+    xs, dts, Bs, Cs = O.make_inputs(b, H, P, G, N, steps, seed=seed, io_dtype=torch.bfloat16)
+    s0 = state0(b, H, P, N, seed)
+    mixer = types.SimpleNamespace(v4cfg=dict(pb=pb, c=c, cold="fp8"), _v4buf=None, num_heads=H,
+                                  D=prm["D"], dt_bias=prm["dt_bias"], A=prm["A"])
+    ssm = torch.zeros(S, H, P, N)
+    ssm[slots] = s0
+    VP.prefill_snapshot(mixer, ssm, slots)
+    buf = mixer._v4buf
+    arrays = dict(pre_codes=buf["snap"][slots].view(torch.uint8).clone(),
+                  pre_scale=buf["scale"][slots][..., 0].clone())
+    ys, ts, glogs, flush_codes, flush_scale = [], [], [], [], []
+    HG = H // G
+    for s in range(steps):
+        # the fresh update selective_state_update performs before decode_readout (no dt clamp)
+        dt = torch.nn.functional.softplus(dts[s].float() + prm["dt_bias"].view(1, -1))
+        dA = dt * prm["A"].view(1, -1)
+        Bh = Bs[s].float().repeat_interleave(HG, dim=1)
+        x = xs[s].float()
+        st = ssm[slots]
+        st = st * torch.exp(dA)[:, :, None, None] + (dt[:, :, None, None] * Bh[:, :, None, :]) * x[..., None]
+        ssm[slots] = st
+        out = torch.zeros(b, H, P)
+        VP.decode_readout(mixer, ssm, out, xs[s], dts[s], Cs[s], slots)
+        ys.append(out.clone())
+        ts.append(buf["t"][slots].clone())
+        glogs.append(buf["glog"][slots].clone())
+        if (s + 1) % c == 0:
+            flush_codes.append(buf["snap"][slots].view(torch.uint8).clone())
+            flush_scale.append(buf["scale"][slots][..., 0].clone())
+    arrays.update(y=torch.stack(ys), t=torch.stack(ts), glog=torch.stack(glogs),
+                  flush_codes=torch.stack(flush_codes), flush_scale=torch.stack(flush_scale),
+                  A=prm["A"], D=prm["D"], dt_bias=prm["dt_bias"])
+    for k, v in dict(x=xs, dt=dts, B=Bs, C=Cs, s0=s0).items():
+        arrays[f"sum_{k}"] = torch.tensor(checksum(v), dtype=torch.float64)
+    return arrays
+
+
+def make_rot(ref):
+    sys.path.insert(0, os.path.join(ref, "scale"))
+    import vllm_v4_patch as VP
+    T, G, N, seed = ROT["T"], ROT["G"], ROT["N"], ROT["seed"]
+    g = torch.Generator().manual_seed(seed)
+    x = (torch.randn(T, G * N, generator=g) / math.sqrt(N)).to(torch.bfloat16)
+    R = torch.linalg.qr(torch.randn(G, N, N, generator=g))[0].contiguous().float()
+    return dict(x=x.view(torch.int16), R=R, out_bf16=VP.rot_flat(x, R).view(torch.int16),
+                out_fp32=VP.rot_flat(x.float(), R))
+
+
+def save(name, arrays):
+    np_arrays = {k: (v.view(torch.int16) if v.dtype == torch.bfloat16 else v).numpy() for k, v in arrays.items()}
+    path = os.path.join(HERE, name)
+    np.savez_compressed(path, **np_arrays)
+    print(f"wrote {path} ({os.path.getsize(path) / 1024:.0f} KiB)")
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", required=True, help="checkout of omin-Kwon/nested_ssm")
+    a = ap.parse_args()
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    with torch.no_grad():
+        save("native_decode_fp32.npz", make_native(a.reference))
+        save("vllm_fp8.npz", make_vllm(a.reference))
+        save("rot_flat.npz", make_rot(a.reference))
+
+
+if __name__ == "__main__":
+    main()

@@ -120,6 +120,24 @@ def test_config0_fp32_64_steps_with_rotation():
     Hh.compare_pool(gpool, opool, 0, slots, "fp32", hot_rtol=1e-4, hot_atol=1e-5)
 
 
+@pytest.mark.parametrize("c,P", [(2, 80), (8, 80), (16, 80), (4, 64), (8, 64), (16, 64), (4, 48)])
+def test_chunk_and_headdim_instances(c, P):
+    """The production configuration (fp8 cold, bf16 io) has kernels with c and
+    headdim fixed at compile time (c in {4, 8, 16}, headdim in {64, 80}); the others
+    read them at run time.  Per-step parity from identical state across two flushes."""
+    steps = 2 * c + 1
+    case = Hh.make_case(b=6, S=9, P=P, pb=32, c=c, cold="fp8", steps=steps, seed=40 + c + P)
+    opool, gpool = Hh.oracle_pool(case), Hh.gpu_pool(case)
+    slots = torch.tensor([4, 8, 0, 2, 7, 1])
+    _split_both(case, gpool, opool, slots)
+    for s in range(steps):
+        Hh.sync_oracle_from_gpu(gpool, opool)
+        yg, yo = Hh.step_both(case, gpool, opool, s, slots, use_gpu_rotation=(s % 2 == 0))
+        Hh.assert_y_close(yg, yo, f"step {s}")
+        Hh.compare_pool(gpool, opool, 0, slots, "fp8", max_ulp=1, max_ulp_frac=1e-4)
+        torch.testing.assert_close(gpool.ring_dt[0].cpu()[slots][..., :c], opool.ring_dt[slots], rtol=1e-6, atol=0)
+
+
 def test_ragged_pad_and_phase_offsets():
     """Padded rows (slot -1) are skipped and leave out untouched; slots enter at
     different times so each flushes on its own t % c."""

@@ -131,20 +131,17 @@ int check_args(const nssm_step_args* a, int H) {
   return NSSM_OK;
 }
 
-// The rotation kernel stages R[g] (66 KB) in shared memory: opt in once per device.
-int ensure_rot_attr(size_t smem) {
-  static std::atomic<uint64_t> done{0};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return cuda_check("cudaGetDevice");
-  const uint64_t bit = 1ull << (dev & 63);
-  if (done.load(std::memory_order_acquire) & bit) return NSSM_OK;
-  if (cudaFuncSetAttribute(nssm::rot_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-    return cuda_check("cudaFuncSetAttribute(rot_kernel)");
-  done.fetch_or(bit, std::memory_order_acq_rel);
-  return NSSM_OK;
+// Rotate B and C into the workspace (if R given); fills sp.B / sp.C.
+int launch_rot(const nssm::RotParams& rp, int rows_total, int G, cudaStream_t st) {
+  int sms = 0;
+  int rc = sm_count(&sms);
+  if (rc) return rc;
+  const int rb = nssm::rot_rows_per_block(rows_total, G, sms);
+  dim3 grid((unsigned)((rows_total + rb - 1) / rb), (unsigned)G, 1);
+  nssm::rot_kernel<128><<<grid, nssm::kRotThreads, 0, st>>>(rp, rows_total, rb);
+  return cuda_check("rot_kernel launch");
 }
 
-// Rotate B and C into the workspace (if R given); fills sp.B / sp.C.
 int maybe_rotate(const nssm_step_args* a, int G, int N, nssm::StepParams& sp, cudaStream_t st) {
   sp.B = a->B; sp.B_sb = a->B_stride_b;
   sp.C = a->C; sp.C_sb = a->C_stride_b;
@@ -153,21 +150,15 @@ int maybe_rotate(const nssm_step_args* a, int G, int N, nssm::StepParams& sp, cu
   if (!a->workspace || a->workspace_bytes < need)
     return fail(NSSM_ERR_INVALID, "workspace of %zu bytes needed for the rotation (got %zu)", need, a->workspace_bytes);
   if (N != 128) return fail(NSSM_ERR_UNSUPPORTED, "rotation compiled for dstate 128 only");
+  if (reinterpret_cast<uintptr_t>(a->R) % 16) return fail(NSSM_ERR_INVALID, "R must be 16-byte aligned");
   const size_t half = need / 2;
-  int rc0;
   nssm::RotParams rp{};
   rp.x0 = a->B; rp.xs0 = a->B_stride_b;
   rp.x1 = a->C; rp.xs1 = a->C_stride_b;
   rp.o0 = a->workspace; rp.os0 = (int64_t)G * N;
   rp.o1 = static_cast<char*>(a->workspace) + half; rp.os1 = (int64_t)G * N;
   rp.R = a->R; rp.T = a->batch; rp.G = G; rp.dtype = a->io_dtype;
-  rp.idx = a->state_batch_indices; rp.pad = a->pad_slot_id;
-  const size_t smem = sizeof(float) * (128 * 129 + nssm::kRotRows * 128);
-  rc0 = ensure_rot_attr(smem);
-  if (rc0) return rc0;
-  dim3 grid((a->batch + nssm::kRotRows - 1) / nssm::kRotRows, G, 2);
-  nssm::rot_kernel<128><<<grid, 128, smem, st>>>(rp);
-  int rc = cuda_check("rot_kernel launch");
+  int rc = launch_rot(rp, 2 * a->batch, G, st);
   if (rc) return rc;
   sp.B = rp.o0; sp.B_sb = rp.os0;
   sp.C = rp.o1; sp.C_sb = rp.os1;
@@ -277,22 +268,18 @@ int nssm_materialize(const nssm_pool* pool, const float* A, const int32_t* slots
 
 int nssm_rot_flat(const void* x, int64_t x_stride, int32_t dtype, const float* R, int32_t T, int32_t ngroups,
                   int32_t dstate, void* out, int64_t out_stride, void* stream) {
-  if (T < 0 || T > 65535 * nssm::kRotRows) return fail(NSSM_ERR_INVALID, "T %d out of range", T);
+  if (T < 0 || T > (1 << 24)) return fail(NSSM_ERR_INVALID, "T %d out of range", T);
   if (T == 0) return NSSM_OK;
   if (!x || !R || !out) return fail(NSSM_ERR_INVALID, "x / R / out is NULL");
   if (dtype != NSSM_F32 && dtype != NSSM_BF16) return fail(NSSM_ERR_INVALID, "dtype must be F32 or BF16");
   if (dstate != 128) return fail(NSSM_ERR_UNSUPPORTED, "rotation compiled for dstate 128 only");
-  if (ngroups <= 0) return fail(NSSM_ERR_INVALID, "ngroups %d", ngroups);
+  if (ngroups <= 0 || ngroups > 65535) return fail(NSSM_ERR_INVALID, "ngroups %d", ngroups);
+  if (reinterpret_cast<uintptr_t>(R) % 16) return fail(NSSM_ERR_INVALID, "R must be 16-byte aligned");
   nssm::RotParams rp{};
   rp.x0 = rp.x1 = x; rp.xs0 = rp.xs1 = x_stride;
   rp.o0 = rp.o1 = out; rp.os0 = rp.os1 = out_stride;
-  rp.R = R; rp.T = T; rp.G = ngroups; rp.dtype = dtype; rp.idx = nullptr; rp.pad = -1;
-  const size_t smem = sizeof(float) * (128 * 129 + nssm::kRotRows * 128);
-  int rc = ensure_rot_attr(smem);
-  if (rc) return rc;
-  dim3 grid((T + nssm::kRotRows - 1) / nssm::kRotRows, ngroups, 1);
-  nssm::rot_kernel<128><<<grid, 128, smem, static_cast<cudaStream_t>(stream)>>>(rp);
-  return cuda_check("rot_kernel launch");
+  rp.R = R; rp.T = T; rp.G = ngroups; rp.dtype = dtype;
+  return launch_rot(rp, T, ngroups, static_cast<cudaStream_t>(stream));
 }
 
 int32_t nssm_supported_hot_dims(int32_t dstate, int32_t* widths, int32_t cap) {

@@ -789,62 +789,90 @@ struct RotParams {
   void* o1;
   int64_t os0, os1;
   const float* R;
-  int T, G, dtype;
-  const int32_t* idx;  // optional: rows whose idx == pad are skipped
-  int pad;
+  int T, G, dtype;      // rows [0, T) come from x0 / o0, rows [T, 2T) from x1 / o1
 };
 
-constexpr int kRotRows = 16;
+// Rotation of B and C by R (out[j][g][m] = sum_n R[g][m][n] x[j][g][n], fp32 accumulate).
+// One CTA per (group g, block of up to kRotRB rows of the stacked B;C row list): thread m
+// keeps row m of R_g in registers (loaded once with 128-bit loads), the block's rows are
+// staged in shared memory as fp32 and read back as broadcasts, and each thread produces
+// output m of four rows at a time.
+constexpr int kRotRB = 32;
+constexpr int kRotThreads = 128;
+
+__host__ __device__ inline int rot_rows_per_block(int rows_total, int G, int sms) {
+  // about two blocks per SM, at most kRotRB rows, a multiple of 4
+  long long want = ((long long)rows_total * G + 2LL * sms - 1) / (2LL * sms);
+  int rb = (int)((want + 3) / 4 * 4);
+  return rb < 4 ? 4 : (rb > kRotRB ? kRotRB : rb);
+}
 
 template <int N>
-__global__ void __launch_bounds__(N) rot_kernel(const RotParams p) {
-  static_assert(N % 4 == 0, "dstate must be a multiple of 4");
-  extern __shared__ float smem[];
-  float* RT = smem;                    // [N][N+1]: RT[n][m] = R[g][m][n]
-  float* xs = smem + N * (N + 1);      // [kRotRows][N] (16-byte aligned: N*(N+1)*4 % 16 == 0 for N % 4 == 0)
+__global__ void __launch_bounds__(kRotThreads, 3) rot_kernel(const RotParams p, int rows_total, int rb) {
+  static_assert(N == kRotThreads, "one thread per output element");
+  __shared__ __align__(16) float xs[kRotRB][N];
   const int g = blockIdx.y;
-  const int which = blockIdx.z;
-  const void* x = which ? p.x1 : p.x0;
-  void* o = which ? p.o1 : p.o0;
-  const int64_t xst = which ? p.xs1 : p.xs0;
-  const int64_t ost = which ? p.os1 : p.os0;
   const int m = threadIdx.x;
-  const float* Rg = p.R + (int64_t)g * N * N;
-  for (int e = m; e < N * N; e += N) {
-    const int mm = e / N, nn = e - mm * N;
-    RT[nn * (N + 1) + mm] = Rg[e];
-  }
-  const int r0 = blockIdx.x * kRotRows;
-  const int nr = min(kRotRows, p.T - r0);
-  for (int e = m; e < kRotRows * N; e += N) {
-    const int r = e / N, nn = e - r * N;
-    xs[r * N + nn] = (r < nr) ? ld_io(x, (int64_t)(r0 + r) * xst + (int64_t)g * N + nn, p.dtype) : 0.0f;
-  }
-  __syncthreads();
-  float acc[kRotRows];
+  const int j0 = blockIdx.x * rb;
+  const int nr = min(rb, rows_total - j0);
+
+  float Rr[N];
+  const float4* Rg4 = reinterpret_cast<const float4*>(p.R + ((int64_t)g * N + m) * N);
 #pragma unroll
-  for (int r = 0; r < kRotRows; ++r) acc[r] = 0.0f;
-  for (int n = 0; n < N; n += 4) {
-    const float r0v = RT[(n + 0) * (N + 1) + m];
-    const float r1v = RT[(n + 1) * (N + 1) + m];
-    const float r2v = RT[(n + 2) * (N + 1) + m];
-    const float r3v = RT[(n + 3) * (N + 1) + m];
+  for (int q = 0; q < N / 4; ++q) {
+    const float4 v = __ldg(Rg4 + q);
+    Rr[4 * q] = v.x;
+    Rr[4 * q + 1] = v.y;
+    Rr[4 * q + 2] = v.z;
+    Rr[4 * q + 3] = v.w;
+  }
+  // stage the block's rows as fp32 (zeros past the end); every load is issued before
+  // the first store so their latencies overlap
+  constexpr int kStageIt = kRotRB * (N / 2) / kRotThreads;
+  float2 v[kStageIt];
 #pragma unroll
-    for (int r = 0; r < kRotRows; ++r) {
-      const float4 xv = *reinterpret_cast<const float4*>(xs + r * N + n);
-      float a = acc[r];
-      a = fmaf(r0v, xv.x, a);
-      a = fmaf(r1v, xv.y, a);
-      a = fmaf(r2v, xv.z, a);
-      a = fmaf(r3v, xv.w, a);
-      acc[r] = a;
+  for (int it = 0; it < kStageIt; ++it) {
+    const int e = m + it * kRotThreads;
+    const int r = e / (N / 2), n = 2 * (e - r * (N / 2));
+    v[it] = make_float2(0.0f, 0.0f);
+    if (r < nr) {
+      const int j = j0 + r;
+      const bool second = j >= p.T;
+      const void* x = second ? p.x1 : p.x0;
+      const int64_t i = (int64_t)(second ? j - p.T : j) * (second ? p.xs1 : p.xs0) + (int64_t)g * N + n;
+      v[it] = make_float2(ld_io(x, i, p.dtype), ld_io(x, i + 1, p.dtype));   // strides may be odd
     }
   }
 #pragma unroll
-  for (int r = 0; r < kRotRows; ++r) {
-    if (r >= nr) break;
-    if (p.idx && p.idx[r0 + r] == p.pad) continue;
-    st_io(o, (int64_t)(r0 + r) * ost + (int64_t)g * N + m, p.dtype, acc[r]);
+  for (int it = 0; it < kStageIt; ++it) {
+    const int e = m + it * kRotThreads;
+    const int r = e / (N / 2), n = 2 * (e - r * (N / 2));
+    *reinterpret_cast<float2*>(&xs[r][n]) = v[it];
+  }
+  __syncthreads();
+  for (int r = 0; r < nr; r += 4) {
+    // one fused multiply-add chain per row in n order (the order of a plain fp32 dot product)
+    float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int q = 0; q < N / 4; ++q) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float4 xv = *reinterpret_cast<const float4*>(&xs[r + i][4 * q]);
+        a[i] = fmaf(Rr[4 * q], xv.x, a[i]);
+        a[i] = fmaf(Rr[4 * q + 1], xv.y, a[i]);
+        a[i] = fmaf(Rr[4 * q + 2], xv.z, a[i]);
+        a[i] = fmaf(Rr[4 * q + 3], xv.w, a[i]);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (r + i >= nr) break;
+      const int j = j0 + r + i;
+      const bool second = j >= p.T;
+      const int row = second ? j - p.T : j;   // padded rows are rotated too (nobody reads them)
+      void* o = second ? p.o1 : p.o0;
+      st_io(o, (int64_t)row * (second ? p.os1 : p.os0) + (int64_t)g * N + m, p.dtype, a[i]);
+    }
   }
 }
 

@@ -8,7 +8,7 @@ reference's own code (tests/golden/make_golden.py), with no oracle in between.
 * ``decode_readout`` with fp8 cold: y within the parity bar, t exact and glog within
   fp32 rounding until the first flush (after it the fp8-only cold master drifts from the
   fp32 master by design; the oracle tests cover the replay).
-* rotation: within one bf16 ulp of ``rot_flat`` in fp32, rarely differing.
+* rotation: within one ulp plus the fp32 dot-product rounding bound of ``rot_flat`` in fp32.
 """
 import pytest
 import torch
@@ -51,14 +51,8 @@ def test_rotation_golden():
     from nested_ssm_b200 import rot_flat
     d = GD.load("rot_flat.npz")
     x, R = GD.bf16(d["x"]).cuda(), d["R"].cuda()
-    got = rot_flat(x, R).cpu()
-    want = d["out_fp32"].to(torch.bfloat16)
-    dist = Hh.bf16_ulp_dist(got, want)
-    assert int(dist.max()) <= 1
-    assert float((dist > 0).float().mean()) <= 1e-2
-    # fp32 output: fp32 accumulation in another order
-    got32 = rot_flat(x.float(), R).cpu()
-    torch.testing.assert_close(got32, d["out_fp32"], rtol=1e-5, atol=1e-6)
+    Hh.rotation_close(rot_flat(x, R).cpu(), d["out_fp32"].to(torch.bfloat16), x.cpu(), R.cpu())
+    Hh.rotation_close(rot_flat(x.float(), R).cpu(), d["out_fp32"], x.cpu(), R.cpu())
 
 
 def test_vllm_fp8_golden():

@@ -135,7 +135,6 @@ def test_chunk_and_headdim_instances(c, P):
         yg, yo = Hh.step_both(case, gpool, opool, s, slots, use_gpu_rotation=(s % 2 == 0))
         Hh.assert_y_close(yg, yo, f"step {s}")
         Hh.compare_pool(gpool, opool, 0, slots, "fp8", max_ulp=1, max_ulp_frac=1e-4)
-        torch.testing.assert_close(gpool.ring_dt[0].cpu()[slots][..., :c], opool.ring_dt[slots], rtol=1e-6, atol=0)
 
 
 def test_ragged_pad_and_phase_offsets():
@@ -226,13 +225,7 @@ def test_rot_flat(dtype):
     x = (torch.randn(37, 8 * 128) / 11.3).to(dtype)
     yo = O.rot_flat(x, prm["R"], "fp32")
     yg = rot_flat(x.cuda(), prm["R"].cuda()).cpu()
-    if dtype == torch.float32:
-        torch.testing.assert_close(yg, yo, rtol=1e-5, atol=1e-6)
-    else:
-        diff = (yg.float() - yo.float()).abs()
-        ulp = yo.float().abs() * 2.0 ** -7 + 1e-30
-        assert bool((diff <= ulp).all()), "bf16 rotation differs by more than 1 ulp"
-        assert float((diff > 0).float().mean()) < 0.02
+    Hh.rotation_close(yg, yo, x, prm["R"])
 
 
 def test_materialize_matches_oracle_and_native():

@@ -133,12 +133,19 @@ int check_args(const nssm_step_args* a, int H) {
 
 // Rotate B and C into the workspace (if R given); fills sp.B / sp.C.
 int launch_rot(const nssm::RotParams& rp, int rows_total, int G, cudaStream_t st) {
-  int sms = 0;
-  int rc = sm_count(&sms);
-  if (rc) return rc;
-  const int rb = nssm::rot_rows_per_block(rows_total, G, sms);
-  dim3 grid((unsigned)((rows_total + rb - 1) / rb), (unsigned)G, 1);
-  nssm::rot_kernel<128><<<grid, nssm::kRotThreads, 0, st>>>(rp, rows_total, rb);
+  // 80 KB of dynamic shared memory: opt in once per device
+  static std::atomic<unsigned long long> attr_done{0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return cuda_check("cudaGetDevice");
+  const unsigned long long bit = 1ull << (dev & 63);
+  constexpr int smem = nssm::rot_smem_bytes(128);
+  if (!(attr_done.load(std::memory_order_acquire) & bit)) {
+    if (cudaFuncSetAttribute(nssm::rot_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+      return cuda_check("cudaFuncSetAttribute(rot_kernel)");
+    attr_done.fetch_or(bit, std::memory_order_acq_rel);
+  }
+  dim3 grid((unsigned)((rows_total + nssm::kRotTile - 1) / nssm::kRotTile), (unsigned)G, 1);
+  nssm::rot_kernel<128><<<grid, nssm::kRotThreads, smem, st>>>(rp, rows_total);
   return cuda_check("rot_kernel launch");
 }
 

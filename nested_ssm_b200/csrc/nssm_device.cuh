@@ -792,86 +792,106 @@ struct RotParams {
   int T, G, dtype;      // rows [0, T) come from x0 / o0, rows [T, 2T) from x1 / o1
 };
 
-// Rotation of B and C by R (out[j][g][m] = sum_n R[g][m][n] x[j][g][n], fp32 accumulate).
-// One CTA per (group g, block of up to kRotRB rows of the stacked B;C row list): thread m
-// keeps row m of R_g in registers (loaded once with 128-bit loads), the block's rows are
-// staged in shared memory as fp32 and read back as broadcasts, and each thread produces
-// output m of four rows at a time.
-constexpr int kRotRB = 32;
+// Rotation of B and C by R (out[j][g][m] = sum_n R[g][m][n] x[j][g][n], fp32 accumulate,
+// n in order).  Per group a small GEMM OUT[rows][m] = X[rows][n] R_g^T[n][m]: one CTA per
+// (group g, tile of kRotTile rows of the stacked B;C row list) stages R_g^T (64 KB) and the
+// tile's X^T (16 KB) in shared memory, and every thread accumulates a 4-row x 8-output
+// register tile, so each value read from shared memory feeds 4 or 8 FMAs.
+constexpr int kRotTile = 32;
 constexpr int kRotThreads = 128;
 
-__host__ __device__ inline int rot_rows_per_block(int rows_total, int G, int sms) {
-  // about two blocks per SM, at most kRotRB rows, a multiple of 4
-  long long want = ((long long)rows_total * G + 2LL * sms - 1) / (2LL * sms);
-  int rb = (int)((want + 3) / 4 * 4);
-  return rb < 4 ? 4 : (rb > kRotRB ? kRotRB : rb);
-}
+__host__ __device__ constexpr int rot_smem_bytes(int N) { return (N * N + N * kRotTile) * 4; }
 
 template <int N>
-__global__ void __launch_bounds__(kRotThreads, 3) rot_kernel(const RotParams p, int rows_total, int rb) {
-  static_assert(N == kRotThreads, "one thread per output element");
-  __shared__ __align__(16) float xs[kRotRB][N];
+__global__ void __launch_bounds__(kRotThreads, 2) rot_kernel(const RotParams p, int rows_total) {
+  static_assert(N == 128, "tile mapping assumes dstate 128");
+  extern __shared__ __align__(16) float rsm[];
+  float* RT = rsm;              // [N][N]: RT[n][m] = R[g][m][n]
+  float* XT = rsm + N * N;      // [N][kRotTile]: XT[n][r] = x[j0 + r][g][n]
   const int g = blockIdx.y;
-  const int m = threadIdx.x;
-  const int j0 = blockIdx.x * rb;
-  const int nr = min(rb, rows_total - j0);
+  const int tid = threadIdx.x;
+  const int j0 = blockIdx.x * kRotTile;
+  const int nr = min(kRotTile, rows_total - j0);
 
-  float Rr[N];
-  const float4* Rg4 = reinterpret_cast<const float4*>(p.R + ((int64_t)g * N + m) * N);
+  // R_g^T: thread m reads row m of R_g (128-bit loads, 8 in flight) and scatters it down
+  // column m of RT (consecutive threads -> consecutive banks)
+  {
+    const int m = tid;
+    const float4* src = reinterpret_cast<const float4*>(p.R + ((int64_t)g * N + m) * N);
 #pragma unroll
-  for (int q = 0; q < N / 4; ++q) {
-    const float4 v = __ldg(Rg4 + q);
-    Rr[4 * q] = v.x;
-    Rr[4 * q + 1] = v.y;
-    Rr[4 * q + 2] = v.z;
-    Rr[4 * q + 3] = v.w;
-  }
-  // stage the block's rows as fp32 (zeros past the end); every load is issued before
-  // the first store so their latencies overlap
-  constexpr int kStageIt = kRotRB * (N / 2) / kRotThreads;
-  float2 v[kStageIt];
+    for (int q0 = 0; q0 < N / 4; q0 += 8) {
+      float4 v[8];
 #pragma unroll
-  for (int it = 0; it < kStageIt; ++it) {
-    const int e = m + it * kRotThreads;
-    const int r = e / (N / 2), n = 2 * (e - r * (N / 2));
-    v[it] = make_float2(0.0f, 0.0f);
-    if (r < nr) {
-      const int j = j0 + r;
-      const bool second = j >= p.T;
-      const void* x = second ? p.x1 : p.x0;
-      const int64_t i = (int64_t)(second ? j - p.T : j) * (second ? p.xs1 : p.xs0) + (int64_t)g * N + n;
-      v[it] = make_float2(ld_io(x, i, p.dtype), ld_io(x, i + 1, p.dtype));   // strides may be odd
-    }
-  }
+      for (int u = 0; u < 8; ++u) v[u] = __ldg(src + q0 + u);
 #pragma unroll
-  for (int it = 0; it < kStageIt; ++it) {
-    const int e = m + it * kRotThreads;
-    const int r = e / (N / 2), n = 2 * (e - r * (N / 2));
-    *reinterpret_cast<float2*>(&xs[r][n]) = v[it];
-  }
-  __syncthreads();
-  for (int r = 0; r < nr; r += 4) {
-    // one fused multiply-add chain per row in n order (the order of a plain fp32 dot product)
-    float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-    for (int q = 0; q < N / 4; ++q) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float4 xv = *reinterpret_cast<const float4*>(&xs[r + i][4 * q]);
-        a[i] = fmaf(Rr[4 * q], xv.x, a[i]);
-        a[i] = fmaf(Rr[4 * q + 1], xv.y, a[i]);
-        a[i] = fmaf(Rr[4 * q + 2], xv.z, a[i]);
-        a[i] = fmaf(Rr[4 * q + 3], xv.w, a[i]);
+      for (int u = 0; u < 8; ++u) {
+        const int n = 4 * (q0 + u);
+        RT[(n + 0) * N + m] = v[u].x;
+        RT[(n + 1) * N + m] = v[u].y;
+        RT[(n + 2) * N + m] = v[u].z;
+        RT[(n + 3) * N + m] = v[u].w;
       }
     }
+  }
+  // X^T: thread (row r = tid % 32, n-pair set tid / 32) loads pairs of its row; zeros past
+  // the end of the row list
+  {
+    const int r = tid % kRotTile;
+    const int j = j0 + r;
+    const bool live = r < nr;
+    const bool second = j >= p.T;
+    const void* x = second ? p.x1 : p.x0;
+    const int64_t base = (int64_t)(second ? j - p.T : j) * (second ? p.xs1 : p.xs0) + (int64_t)g * N;
+    constexpr int kStep = kRotThreads / kRotTile;        // n-pair sets
+    constexpr int kPairs = N / 2 / kStep;                 // pairs per thread
+    float2 v[kPairs];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      if (r + i >= nr) break;
-      const int j = j0 + r + i;
-      const bool second = j >= p.T;
-      const int row = second ? j - p.T : j;   // padded rows are rotated too (nobody reads them)
-      void* o = second ? p.o1 : p.o0;
-      st_io(o, (int64_t)row * (second ? p.os1 : p.os0) + (int64_t)g * N + m, p.dtype, a[i]);
+    for (int u = 0; u < kPairs; ++u) {
+      const int n = 2 * (tid / kRotTile + u * kStep);
+      v[u] = live ? make_float2(ld_io(x, base + n, p.dtype), ld_io(x, base + n + 1, p.dtype))   // strides may be odd
+                  : make_float2(0.0f, 0.0f);
+    }
+#pragma unroll
+    for (int u = 0; u < kPairs; ++u) {
+      const int n = 2 * (tid / kRotTile + u * kStep);
+      XT[n * kRotTile + r] = v[u].x;
+      XT[(n + 1) * kRotTile + r] = v[u].y;
+    }
+  }
+  __syncthreads();
+
+  // thread tile: rows 4*rg .. 4*rg+3, outputs 4*mg .. 4*mg+3 and 64+4*mg .. 64+4*mg+3
+  const int rg = tid / 16, mg = tid % 16;
+  float acc[4][8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+#pragma unroll 4
+  for (int n = 0; n < N; ++n) {
+    const float4 xv = *reinterpret_cast<const float4*>(XT + n * kRotTile + 4 * rg);
+    const float4 ra = *reinterpret_cast<const float4*>(RT + n * N + 4 * mg);
+    const float4 rb = *reinterpret_cast<const float4*>(RT + n * N + 64 + 4 * mg);
+    const float xs[4] = {xv.x, xv.y, xv.z, xv.w};
+    const float rs[8] = {ra.x, ra.y, ra.z, ra.w, rb.x, rb.y, rb.z, rb.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(rs[j], xs[i], acc[i][j]);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = 4 * rg + i;
+    if (r >= nr) break;
+    const int j = j0 + r;
+    const bool second = j >= p.T;
+    const int row = second ? j - p.T : j;   // padded rows are rotated too (nobody reads them)
+    void* o = second ? p.o1 : p.o0;
+    const int64_t ob = (int64_t)row * (second ? p.os1 : p.os0) + (int64_t)g * N;
+#pragma unroll
+    for (int jj = 0; jj < 8; ++jj) {
+      const int m = jj < 4 ? 4 * mg + jj : 64 + 4 * mg + (jj - 4);
+      st_io(o, ob + m, p.dtype, acc[i][jj]);
     }
   }
 }

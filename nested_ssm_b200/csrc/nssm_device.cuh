@@ -195,6 +195,23 @@ __device__ __forceinline__ void word_to_float(uint32_t word, float* v) {
   }
 }
 
+// The four e4m3 codes of a word as fp32 values scaled by 2^-120, by bit moves only (no
+// conversion unit): the code's sign goes to bit 31 and its 4 exponent + 3 mantissa bits to
+// bits 26..20, so the fp32 exponent field equals the e4m3 exponent field.  A normal e4m3
+// value q = 2^(e-7)(1+m/8) then reads as the normal fp32 2^(e-127)(1+m/8) = q 2^-120, and an
+// e4m3 subnormal 2^-6 (m/8) as the fp32 subnormal 2^-126 (m/8) = q 2^-120: exact for every
+// finite code (the NaN codes, which satfinite quantisation never stores, read as finite).
+// Callers fold 2^120 into another factor, keeping every product exactly rounded once.
+constexpr float kFp8Unscale = 0x1p120f;
+
+__device__ __forceinline__ void fp8x4_to_f32_scaled(uint32_t w, float* v) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint32_t y = __byte_perm(w, 0u, 0x0444u | (uint32_t(k) << 12));   // code k in bits 31..24
+    v[k] = __uint_as_float(uint32_t(int32_t(y) >> 4) & 0x87F00000u);
+  }
+}
+
 // Pack CPT fp32 values (already divided by the row scale for fp8) to storage.
 template <int COLD, int CPT>
 __device__ __forceinline__ void float_to_cold(const float* v, uint32_t* w) {
@@ -794,90 +811,91 @@ struct RotParams {
 
 // Rotation of B and C by R (out[j][g][m] = sum_n R[g][m][n] x[j][g][n], fp32 accumulate,
 // n in order).  Per group a small GEMM OUT[rows][m] = X[rows][n] R_g^T[n][m]: one CTA per
-// (group g, tile of kRotTile rows of the stacked B;C row list) stages R_g^T (64 KB) and the
-// tile's X^T (16 KB) in shared memory, and every thread accumulates a 4-row x 8-output
-// register tile, so each value read from shared memory feeds 4 or 8 FMAs.
+// (group g, tile of kRotTile rows of the stacked B;C row list) copies R_g (64 KB, coalesced
+// 128-bit loads) and the tile's rows (as fp32) into shared memory with rows padded to
+// kRotLd floats, and every thread accumulates a 4-row x 8-output register tile, reading
+// four n at a time, so each 128-bit shared-memory read feeds 16 or 32 FMAs.
 constexpr int kRotTile = 32;
 constexpr int kRotThreads = 128;
+constexpr int kRotLd = 132;   // padded row length: 16-byte aligned, rows 4 banks apart
 
-__host__ __device__ constexpr int rot_smem_bytes(int N) { return (N * N + N * kRotTile) * 4; }
+__host__ __device__ constexpr int rot_smem_bytes(int N) { return (N + kRotTile) * kRotLd * 4; }
 
 template <int N>
 __global__ void __launch_bounds__(kRotThreads, 2) rot_kernel(const RotParams p, int rows_total) {
   static_assert(N == 128, "tile mapping assumes dstate 128");
   extern __shared__ __align__(16) float rsm[];
-  float* RT = rsm;              // [N][N]: RT[n][m] = R[g][m][n]
-  float* XT = rsm + N * N;      // [N][kRotTile]: XT[n][r] = x[j0 + r][g][n]
+  float* Rs = rsm;                  // [N][kRotLd]: Rs[m][n] = R[g][m][n]
+  float* Xs = rsm + N * kRotLd;     // [kRotTile][kRotLd]: Xs[r][n] = x[j0 + r][g][n]
   const int g = blockIdx.y;
   const int tid = threadIdx.x;
   const int j0 = blockIdx.x * kRotTile;
   const int nr = min(kRotTile, rows_total - j0);
 
-  // R_g^T: thread m reads row m of R_g (128-bit loads, 8 in flight) and scatters it down
-  // column m of RT (consecutive threads -> consecutive banks)
+  // R_g: a warp copies one 512-byte row per instruction (8 loads in flight per thread)
   {
-    const int m = tid;
-    const float4* src = reinterpret_cast<const float4*>(p.R + ((int64_t)g * N + m) * N);
+    const float4* src = reinterpret_cast<const float4*>(p.R + (int64_t)g * N * N);
+    constexpr int kVec = N * N / 4 / kRotThreads;   // float4 per thread
 #pragma unroll
-    for (int q0 = 0; q0 < N / 4; q0 += 8) {
+    for (int u0 = 0; u0 < kVec; u0 += 8) {
       float4 v[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) v[u] = __ldg(src + q0 + u);
+      for (int u = 0; u < 8; ++u) v[u] = __ldg(src + tid + (u0 + u) * kRotThreads);
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
-        const int n = 4 * (q0 + u);
-        RT[(n + 0) * N + m] = v[u].x;
-        RT[(n + 1) * N + m] = v[u].y;
-        RT[(n + 2) * N + m] = v[u].z;
-        RT[(n + 3) * N + m] = v[u].w;
+        const int e = tid + (u0 + u) * kRotThreads;   // float4 index: row e / 32, column 4 * (e % 32)
+        *reinterpret_cast<float4*>(Rs + (e / (N / 4)) * kRotLd + 4 * (e % (N / 4))) = v[u];
       }
     }
   }
-  // X^T: thread (row r = tid % 32, n-pair set tid / 32) loads pairs of its row; zeros past
-  // the end of the row list
+  // the tile's rows: a warp reads one row's 128 values (zeros past the end of the list)
   {
-    const int r = tid % kRotTile;
-    const int j = j0 + r;
-    const bool live = r < nr;
-    const bool second = j >= p.T;
-    const void* x = second ? p.x1 : p.x0;
-    const int64_t base = (int64_t)(second ? j - p.T : j) * (second ? p.xs1 : p.xs0) + (int64_t)g * N;
-    constexpr int kStep = kRotThreads / kRotTile;        // n-pair sets
-    constexpr int kPairs = N / 2 / kStep;                 // pairs per thread
-    float2 v[kPairs];
+    const int warp = tid / 32, lane = tid % 32;
+    constexpr int kRowsPerWarp = kRotTile / (kRotThreads / 32);
+    float v[kRowsPerWarp][4];
 #pragma unroll
-    for (int u = 0; u < kPairs; ++u) {
-      const int n = 2 * (tid / kRotTile + u * kStep);
-      v[u] = live ? make_float2(ld_io(x, base + n, p.dtype), ld_io(x, base + n + 1, p.dtype))   // strides may be odd
-                  : make_float2(0.0f, 0.0f);
+    for (int u = 0; u < kRowsPerWarp; ++u) {
+      const int r = warp * kRowsPerWarp + u;
+      const int j = j0 + r;
+      const bool second = j >= p.T;
+      const void* x = second ? p.x1 : p.x0;
+      const int64_t base = (int64_t)(second ? j - p.T : j) * (second ? p.xs1 : p.xs0) + (int64_t)g * N;
+#pragma unroll
+      for (int t = 0; t < 4; ++t)
+        v[u][t] = r < nr ? ld_io(x, base + lane + 32 * t, p.dtype) : 0.0f;   // strides may be odd
     }
 #pragma unroll
-    for (int u = 0; u < kPairs; ++u) {
-      const int n = 2 * (tid / kRotTile + u * kStep);
-      XT[n * kRotTile + r] = v[u].x;
-      XT[(n + 1) * kRotTile + r] = v[u].y;
-    }
+    for (int u = 0; u < kRowsPerWarp; ++u)
+#pragma unroll
+      for (int t = 0; t < 4; ++t) Xs[(warp * kRowsPerWarp + u) * kRotLd + lane + 32 * t] = v[u][t];
   }
   __syncthreads();
 
-  // thread tile: rows 4*rg .. 4*rg+3, outputs 4*mg .. 4*mg+3 and 64+4*mg .. 64+4*mg+3
+  // thread tile: rows 4*rg .. 4*rg+3, outputs mg + 16*j (j = 0..7)
   const int rg = tid / 16, mg = tid % 16;
   float acc[4][8];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
-#pragma unroll 4
-  for (int n = 0; n < N; ++n) {
-    const float4 xv = *reinterpret_cast<const float4*>(XT + n * kRotTile + 4 * rg);
-    const float4 ra = *reinterpret_cast<const float4*>(RT + n * N + 4 * mg);
-    const float4 rb = *reinterpret_cast<const float4*>(RT + n * N + 64 + 4 * mg);
-    const float xs[4] = {xv.x, xv.y, xv.z, xv.w};
-    const float rs[8] = {ra.x, ra.y, ra.z, ra.w, rb.x, rb.y, rb.z, rb.w};
+#pragma unroll 2
+  for (int n = 0; n < N; n += 4) {
+    float4 xv[4], rv[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) xv[i] = *reinterpret_cast<const float4*>(Xs + (4 * rg + i) * kRotLd + n);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) rv[j] = *reinterpret_cast<const float4*>(Rs + (mg + 16 * j) * kRotLd + n);
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
-      for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(rs[j], xs[i], acc[i][j]);
+      for (int j = 0; j < 8; ++j) {
+        float a = acc[i][j];
+        a = fmaf(rv[j].x, xv[i].x, a);
+        a = fmaf(rv[j].y, xv[i].y, a);
+        a = fmaf(rv[j].z, xv[i].z, a);
+        a = fmaf(rv[j].w, xv[i].w, a);
+        acc[i][j] = a;
+      }
   }
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
@@ -889,10 +907,7 @@ __global__ void __launch_bounds__(kRotThreads, 2) rot_kernel(const RotParams p, 
     void* o = second ? p.o1 : p.o0;
     const int64_t ob = (int64_t)row * (second ? p.os1 : p.os0) + (int64_t)g * N;
 #pragma unroll
-    for (int jj = 0; jj < 8; ++jj) {
-      const int m = jj < 4 ? 4 * mg + jj : 64 + 4 * mg + (jj - 4);
-      st_io(o, ob + m, p.dtype, acc[i][jj]);
-    }
+    for (int jj = 0; jj < 8; ++jj) st_io(o, ob + mg + 16 * jj, p.dtype, acc[i][jj]);
   }
 }
 

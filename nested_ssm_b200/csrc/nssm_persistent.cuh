@@ -91,6 +91,11 @@ __device__ __forceinline__ void bulk_s2g(void* dst, const void* src, uint32_t by
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // the shared-memory sources of all committed bulk stores have been read
 __device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+
+// wait until at most the most recent bulk group of this thread still reads shared memory
+__device__ __forceinline__ void bulk_wait_read_1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
 // all committed bulk stores are complete
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
@@ -266,6 +271,12 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
   constexpr int HQ = (RPWMAX * LPR + 31) / 32;                // hot chunks per lane
   constexpr int CQ = (RPWMAX * CPR + 31) / 32;                // cold chunks per lane (STEP)
   constexpr int CQF = (CPR + (32 / RPWMAX) - 1) / (32 / RPWMAX);   // column passes (FLUSH)
+  // FLUSH of fp8 instances with a compile-time band of an even number of rows: a lane owns
+  // one cold chunk column of two rows (rows rp and rp + RPWC/2 of the band), so the ring's
+  // B'_cold chunk is read once for both rows, and fp8 codes are widened by bit moves
+  // (fp8x4_to_f32_scaled) instead of the conversion unit
+  constexpr bool kPair = COLD == COLD_FP8 && RPWC > 0 && RPWC % 2 == 0 && (RPWC / 2) * CPR <= 32;
+  constexpr int kHR = kPair ? RPWC / 2 : 1;
   static_assert(32 % LPR == 0, "hot row chunks must tile a warp");
   static_assert(COLD != COLD_NONE && NC > 0, "tiered instances only");
   static_assert(CE % 4 == 0 && PB % 4 == 0, "chunk shapes");
@@ -473,6 +484,8 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
   first_valid(q);
   int s = 0;
   uint32_t par = 0;   // stage s / its phase parity for item k
+  int s_prev = 0;
+  uint32_t par_prev = 0;   // FLUSH: stage / parity of item k - 1 (released after item k)
   for (uint32_t k = 0; q.b * H + q.h < end; advance(q), ++k) {
     const int j0b = q.b - b0, b = q.b, h = q.h, g = q.g;
     const int slot = bslot[j0b], tnew = btn[j0b];
@@ -659,96 +672,196 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
       const float* rbp = ring_st ? reinterpret_cast<const float*>(st + L.s_rb)
                                  : p.ring_b + ((int64_t)slot * p.G + g) * c * NC;
       uint4* cst = reinterpret_cast<uint4*>(sm + s * L.stage_bytes + L.s_cold);   // requantised in place
-      // lane -> (row frr of the band, chunk column u*fcw + fcq): the 8 lanes of a
-      // shared-memory phase share a chunk column, so B_j reads are broadcasts
-      float v[CQF][CE];
+      if constexpr (kPair) {
+        // lane -> chunk column cc of rows rA = r0 + rp and rB = rA + RPWC/2: each B_j chunk
+        // read from shared memory serves both rows
+        const int rp = lane % kHR, cc = lane / kHR;
+        const bool act = cc < CPR;
+        const int rA = r0 + rp, rB = rA + kHR;
+        float va[CE], vb[CE];
 #pragma unroll
-      for (int u = 0; u < CQF; ++u) {
-        if (u * fcw >= CPR) break;   // uniform
-        const int cc0 = u * fcw + fcq;
-        const bool act = fok && cc0 < CPR;
-        const int cc = act ? cc0 : 0;
-        const int row = r0 + (fok ? frr : 0);
-        const int i = row * CPR + cc;
+        for (int e = 0; e < CE; ++e) { va[e] = 0.0f; vb[e] = 0.0f; }
+        if (act) {
 #pragma unroll
-        for (int e = 0; e < CE; ++e) v[u][e] = 0.0f;
-#pragma unroll 4
-        for (int j = 0; j < c; ++j) {
-          const float Wv = sW[j * Pn + row];
-          const float2 W2 = f2(Wv, Wv);
-          const float4* b4 = reinterpret_cast<const float4*>(rbp + j * NC + cc * CE);
+          for (int j = 0; j < CFIX; ++j) {
+            const float wa = sW[j * Pn + rA], wb = sW[j * Pn + rB];
+            const float2 wa2 = f2(wa, wa), wb2 = f2(wb, wb);
+            const float4* b4 = reinterpret_cast<const float4*>(rbp + j * NC + cc * CE);
 #pragma unroll
-          for (int e = 0; e < CE / 4; ++e) {
-            const float4 bv = b4[e];
-            const float2 lo = __ffma2_rn(W2, f2(bv.x, bv.y), f2(v[u][4 * e], v[u][4 * e + 1]));
-            const float2 hi = __ffma2_rn(W2, f2(bv.z, bv.w), f2(v[u][4 * e + 2], v[u][4 * e + 3]));
-            v[u][4 * e] = lo.x; v[u][4 * e + 1] = lo.y; v[u][4 * e + 2] = hi.x; v[u][4 * e + 3] = hi.y;
-          }
-        }
-        const float scl = (COLD == COLD_FP8) ? scl_s[row] : 1.0f;
-        const uint4 q4 = csm[i];
-        const uint32_t wv[4] = {q4.x, q4.y, q4.z, q4.w};
-        const float2 e2 = f2(etot, etot), s2 = f2(scl, scl);
-        float m = 0.0f;
-#pragma unroll
-        for (int wi = 0; wi < 4; ++wi) {
-          float qv[kPerW];
-          word_to_float<COLD>(wv[wi], qv);
-          if constexpr (kPerW >= 2) {
-#pragma unroll
-            for (int e = 0; e < kPerW; e += 2) {
-              const int x = wi * kPerW + e;
-              float2 dq = f2(qv[e], qv[e + 1]);
-              if constexpr (COLD == COLD_FP8) dq = __fmul2_rn(dq, s2);
-              const float2 r2 = __fadd2_rn(__fmul2_rn(dq, e2), f2(v[u][x], v[u][x + 1]));
-              v[u][x] = r2.x;
-              v[u][x + 1] = r2.y;
+            for (int e = 0; e < CE / 4; ++e) {
+              const float4 bv = b4[e];
+              const float2 lo = f2(bv.x, bv.y), hi = f2(bv.z, bv.w);
+              float2 t = __ffma2_rn(wa2, lo, f2(va[4 * e], va[4 * e + 1]));
+              va[4 * e] = t.x; va[4 * e + 1] = t.y;
+              t = __ffma2_rn(wa2, hi, f2(va[4 * e + 2], va[4 * e + 3]));
+              va[4 * e + 2] = t.x; va[4 * e + 3] = t.y;
+              t = __ffma2_rn(wb2, lo, f2(vb[4 * e], vb[4 * e + 1]));
+              vb[4 * e] = t.x; vb[4 * e + 1] = t.y;
+              t = __ffma2_rn(wb2, hi, f2(vb[4 * e + 2], vb[4 * e + 3]));
+              vb[4 * e + 2] = t.x; vb[4 * e + 3] = t.y;
             }
-          } else {
-            v[u][wi] = __fadd_rn(__fmul_rn(qv[0], etot), v[u][wi]);
           }
         }
+        // v = (q * scale) * exp(tot) + acc.  q * scale is formed as (q 2^-120)(scale 2^120),
+        // the same product rounded once, while scale 2^120 is finite (scale < 2^7 for every
+        // row of the band; otherwise the conversion-unit path)
+        const float sa = scl_s[rA], sb = scl_s[rB];
+        const bool fast = __all_sync(0xffffffffu, !act || (sa < 128.0f && sb < 128.0f));
+        const float2 e2 = f2(etot, etot);
 #pragma unroll
-        for (int e = 0; e < CE; ++e) m = fmaxf(m, fabsf(v[u][e]));
-        if (COLD == COLD_FP8 && act) pc[i] = m;
-      }
-      if constexpr (COLD == COLD_FP8) {
+        for (int hr = 0; hr < 2; ++hr) {
+          float* v = hr ? vb : va;
+          const float scl = hr ? sb : sa;
+          const int row = hr ? rB : rA;
+          const uint4 q4 = act ? csm[row * CPR + cc] : make_uint4(0u, 0u, 0u, 0u);
+          const uint32_t wv[4] = {q4.x, q4.y, q4.z, q4.w};
+          const float su = fast ? scl * kFp8Unscale : scl;
+          const float2 s2 = f2(su, su);
+          float m = 0.0f;
+#pragma unroll
+          for (int wi = 0; wi < 4; ++wi) {
+            float qv[4];
+            if (fast) fp8x4_to_f32_scaled(wv[wi], qv);
+            else word_to_float<COLD>(wv[wi], qv);
+#pragma unroll
+            for (int e = 0; e < 4; e += 2) {
+              const int x = wi * 4 + e;
+              const float2 dq = __fmul2_rn(f2(qv[e], qv[e + 1]), s2);
+              const float2 r2 = __fadd2_rn(__fmul2_rn(dq, e2), f2(v[x], v[x + 1]));
+              v[x] = r2.x;
+              v[x + 1] = r2.y;
+            }
+          }
+#pragma unroll
+          for (int e = 0; e < CE; ++e) m = fmaxf(m, fabsf(v[e]));
+          if (act) pc[row * CPR + cc] = m;
+        }
         __syncwarp();
         if (lane < nrow) {
           const int row = r0 + lane;
           float m = 0.0f;
 #pragma unroll
-          for (int cc = 0; cc < CPR; ++cc) m = fmaxf(m, pc[row * CPR + cc]);
+          for (int k = 0; k < CPR; ++k) m = fmaxf(m, pc[row * CPR + k]);
           const float sc = __fadd_rn(__fdiv_rn(m, kFp8Max), kScaleEps);
           s_sc[row] = sc;
           s_rcp[row] = __frcp_rn(sc);
           p.scale[sh * Pn + row] = sc;
         }
         __syncwarp();
-      }
+        if (act) {
 #pragma unroll
-      for (int u = 0; u < CQF; ++u) {
-        if (u * fcw >= CPR) break;
-        const int cc0 = u * fcw + fcq;
-        if (fok && cc0 < CPR) {
-          const int row = r0 + frr;
-          if constexpr (COLD == COLD_FP8) {
+          for (int hr = 0; hr < 2; ++hr) {
+            float* v = hr ? vb : va;
+            const int row = hr ? rB : rA;
             // correctly rounded v / scale, two lanes at a time (Markstein's correction)
             const float2 r2 = f2(s_rcp[row], s_rcp[row]);
             const float2 nsc2 = f2(-s_sc[row], -s_sc[row]);
 #pragma unroll
             for (int e = 0; e < CE; e += 2) {
-              const float2 a = f2(v[u][e], v[u][e + 1]);
-              const float2 q0 = __fmul2_rn(a, r2);
-              const float2 rs = __ffma2_rn(q0, nsc2, a);
+              const float2 a2 = f2(v[e], v[e + 1]);
+              const float2 q0 = __fmul2_rn(a2, r2);
+              const float2 rs = __ffma2_rn(q0, nsc2, a2);
               const float2 qq = __ffma2_rn(rs, r2, q0);
-              v[u][e] = qq.x;
-              v[u][e + 1] = qq.y;
+              v[e] = qq.x;
+              v[e + 1] = qq.y;
+            }
+            uint32_t wq[4];
+            float_to_cold<COLD, CE>(v, wq);
+            cst[row * CPR + cc] = make_uint4(wq[0], wq[1], wq[2], wq[3]);
+          }
+        }
+      } else {
+        // lane -> (row frr of the band, chunk column u*fcw + fcq): the 8 lanes of a
+        // shared-memory phase share a chunk column, so B_j reads are broadcasts
+        float v[CQF][CE];
+  #pragma unroll
+        for (int u = 0; u < CQF; ++u) {
+          if (u * fcw >= CPR) break;   // uniform
+          const int cc0 = u * fcw + fcq;
+          const bool act = fok && cc0 < CPR;
+          const int cc = act ? cc0 : 0;
+          const int row = r0 + (fok ? frr : 0);
+          const int i = row * CPR + cc;
+  #pragma unroll
+          for (int e = 0; e < CE; ++e) v[u][e] = 0.0f;
+  #pragma unroll 4
+          for (int j = 0; j < c; ++j) {
+            const float Wv = sW[j * Pn + row];
+            const float2 W2 = f2(Wv, Wv);
+            const float4* b4 = reinterpret_cast<const float4*>(rbp + j * NC + cc * CE);
+  #pragma unroll
+            for (int e = 0; e < CE / 4; ++e) {
+              const float4 bv = b4[e];
+              const float2 lo = __ffma2_rn(W2, f2(bv.x, bv.y), f2(v[u][4 * e], v[u][4 * e + 1]));
+              const float2 hi = __ffma2_rn(W2, f2(bv.z, bv.w), f2(v[u][4 * e + 2], v[u][4 * e + 3]));
+              v[u][4 * e] = lo.x; v[u][4 * e + 1] = lo.y; v[u][4 * e + 2] = hi.x; v[u][4 * e + 3] = hi.y;
             }
           }
-          uint32_t wq[4];
-          float_to_cold<COLD, CE>(v[u], wq);
-          cst[row * CPR + cc0] = make_uint4(wq[0], wq[1], wq[2], wq[3]);
+          const float scl = (COLD == COLD_FP8) ? scl_s[row] : 1.0f;
+          const uint4 q4 = csm[i];
+          const uint32_t wv[4] = {q4.x, q4.y, q4.z, q4.w};
+          const float2 e2 = f2(etot, etot), s2 = f2(scl, scl);
+          float m = 0.0f;
+  #pragma unroll
+          for (int wi = 0; wi < 4; ++wi) {
+            float qv[kPerW];
+            word_to_float<COLD>(wv[wi], qv);
+            if constexpr (kPerW >= 2) {
+  #pragma unroll
+              for (int e = 0; e < kPerW; e += 2) {
+                const int x = wi * kPerW + e;
+                float2 dq = f2(qv[e], qv[e + 1]);
+                if constexpr (COLD == COLD_FP8) dq = __fmul2_rn(dq, s2);
+                const float2 r2 = __fadd2_rn(__fmul2_rn(dq, e2), f2(v[u][x], v[u][x + 1]));
+                v[u][x] = r2.x;
+                v[u][x + 1] = r2.y;
+              }
+            } else {
+              v[u][wi] = __fadd_rn(__fmul_rn(qv[0], etot), v[u][wi]);
+            }
+          }
+  #pragma unroll
+          for (int e = 0; e < CE; ++e) m = fmaxf(m, fabsf(v[u][e]));
+          if (COLD == COLD_FP8 && act) pc[i] = m;
+        }
+        if constexpr (COLD == COLD_FP8) {
+          __syncwarp();
+          if (lane < nrow) {
+            const int row = r0 + lane;
+            float m = 0.0f;
+  #pragma unroll
+            for (int cc = 0; cc < CPR; ++cc) m = fmaxf(m, pc[row * CPR + cc]);
+            const float sc = __fadd_rn(__fdiv_rn(m, kFp8Max), kScaleEps);
+            s_sc[row] = sc;
+            s_rcp[row] = __frcp_rn(sc);
+            p.scale[sh * Pn + row] = sc;
+          }
+          __syncwarp();
+        }
+  #pragma unroll
+        for (int u = 0; u < CQF; ++u) {
+          if (u * fcw >= CPR) break;
+          const int cc0 = u * fcw + fcq;
+          if (fok && cc0 < CPR) {
+            const int row = r0 + frr;
+            if constexpr (COLD == COLD_FP8) {
+              // correctly rounded v / scale, two lanes at a time (Markstein's correction)
+              const float2 r2 = f2(s_rcp[row], s_rcp[row]);
+              const float2 nsc2 = f2(-s_sc[row], -s_sc[row]);
+  #pragma unroll
+              for (int e = 0; e < CE; e += 2) {
+                const float2 a = f2(v[u][e], v[u][e + 1]);
+                const float2 q0 = __fmul2_rn(a, r2);
+                const float2 rs = __ffma2_rn(q0, nsc2, a);
+                const float2 qq = __ffma2_rn(rs, r2, q0);
+                v[u][e] = qq.x;
+                v[u][e + 1] = qq.y;
+              }
+            }
+            uint32_t wq[4];
+            float_to_cold<COLD, CE>(v[u], wq);
+            cst[row * CPR + cc0] = make_uint4(wq[0], wq[1], wq[2], wq[3]);
+          }
         }
       }
       // the band's requantised rows -> global in one bulk store
@@ -761,19 +874,38 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
       }
     }
 
-    // ---- release stage s (after this warp's bulk stores have read it); the producer
-    // refills it once every warp has
+    // ---- release a stage once this warp's bulk store has read it; the producer refills
+    // it once every warp has.  STEP releases the stage it just used.  FLUSH releases the
+    // previous item's stage, so the bulk store of a band overlaps the next item's work.
     __syncwarp();
-    if (lane == 0) {
-      bulk_wait_read_all();
-      mbar_arrive(&empty[s]);
-    }
-    if (tid == 0 && pq.b * H + pq.h < end) {
-      if (!mbar_wait_bounded(&empty[s], par)) { ok = false; break; }
-      fence_proxy_async_smem();
-      issue(pq, s);
-      ++n_issued;
-      advance(pq);
+    if constexpr (STEP) {
+      if (lane == 0) {
+        bulk_wait_read_all();
+        mbar_arrive(&empty[s]);
+      }
+      if (tid == 0 && pq.b * H + pq.h < end) {
+        if (!mbar_wait_bounded(&empty[s], par)) { ok = false; break; }
+        fence_proxy_async_smem();
+        issue(pq, s);
+        ++n_issued;
+        advance(pq);
+      }
+    } else {
+      if (k > 0) {
+        if (lane == 0) {
+          bulk_wait_read_1();
+          mbar_arrive(&empty[s_prev]);
+        }
+        if (tid == 0 && pq.b * H + pq.h < end) {
+          if (!mbar_wait_bounded(&empty[s_prev], par_prev)) { ok = false; break; }
+          fence_proxy_async_smem();
+          issue(pq, s_prev);
+          ++n_issued;
+          advance(pq);
+        }
+      }
+      s_prev = s;
+      par_prev = par;
     }
     if (++s == kStages) { s = 0; par ^= 1u; }
   }

@@ -39,7 +39,7 @@
 #define NSSM_STEP_P_MINB 3
 #endif
 #ifndef NSSM_FLUSH_P_MINB
-#define NSSM_FLUSH_P_MINB 2
+#define NSSM_FLUSH_P_MINB 3
 #endif
 
 namespace nssm {

@@ -195,23 +195,6 @@ __device__ __forceinline__ void word_to_float(uint32_t word, float* v) {
   }
 }
 
-// The four e4m3 codes of a word as fp32 values scaled by 2^-120, by bit moves only (no
-// conversion unit): the code's sign goes to bit 31 and its 4 exponent + 3 mantissa bits to
-// bits 26..20, so the fp32 exponent field equals the e4m3 exponent field.  A normal e4m3
-// value q = 2^(e-7)(1+m/8) then reads as the normal fp32 2^(e-127)(1+m/8) = q 2^-120, and an
-// e4m3 subnormal 2^-6 (m/8) as the fp32 subnormal 2^-126 (m/8) = q 2^-120: exact for every
-// finite code (the NaN codes, which satfinite quantisation never stores, read as finite).
-// Callers fold 2^120 into another factor, keeping every product exactly rounded once.
-constexpr float kFp8Unscale = 0x1p120f;
-
-__device__ __forceinline__ void fp8x4_to_f32_scaled(uint32_t w, float* v) {
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const uint32_t y = __byte_perm(w, 0u, 0x0444u | (uint32_t(k) << 12));   // code k in bits 31..24
-    v[k] = __uint_as_float(uint32_t(int32_t(y) >> 4) & 0x87F00000u);
-  }
-}
-
 // Pack CPT fp32 values (already divided by the row scale for fp8) to storage.
 template <int COLD, int CPT>
 __device__ __forceinline__ void float_to_cold(const float* v, uint32_t* w) {

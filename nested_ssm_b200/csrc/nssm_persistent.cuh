@@ -273,8 +273,8 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
   constexpr int CQF = (CPR + (32 / RPWMAX) - 1) / (32 / RPWMAX);   // column passes (FLUSH)
   // FLUSH of fp8 instances with a compile-time band of an even number of rows: a lane owns
   // one cold chunk column of two rows (rows rp and rp + RPWC/2 of the band), so the ring's
-  // B'_cold chunk is read once for both rows, and fp8 codes are widened by bit moves
-  // (fp8x4_to_f32_scaled) instead of the conversion unit
+  // B'_cold chunk is read once for both rows; the decay and the division by the new row
+  // scale are folded into one multiply each (see the FLUSH body)
   constexpr bool kPair = COLD == COLD_FP8 && RPWC > 0 && RPWC % 2 == 0 && (RPWC / 2) * CPR <= 32;
   constexpr int kHR = kPair ? RPWC / 2 : 1;
   static_assert(32 % LPR == 0, "hot row chunks must tile a warp");
@@ -639,10 +639,11 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
       }
     } else {
       // ---- FLUSH of the band: cold <- exp(sum dA) cold + sum_j exp(suf_j) (dt_j x_j) B_j,
-      // requantised; the ring holds all c tokens of the chunk.  Same operation order as
-      // the oracle: acc = sum_j (W_j * B_j[n]) in j order, mul then add;
-      // v = (q * scale) * exp(tot) + acc; fp8 scale = amax/448 + 1e-12 and
-      // q = rne(v / scale) with a correctly rounded division.
+      // requantised; the ring holds all c tokens of the chunk.  acc = sum_j (W_j * B_j[n])
+      // in j order as the oracle; fp8 scale = amax/448 + 1e-12 exactly as the oracle.  The
+      // general instances also follow the oracle's v = (q * scale) * exp(tot) + acc and
+      // q = rne(v / scale) (correctly rounded division); the paired fp8 instances fold
+      // each into one multiply (below), which moves a stored code by one step, rarely.
       const float A_h = sA[h];
       const bool pre = c <= kRingF32Max;
       if (pre) {
@@ -702,32 +703,27 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
             }
           }
         }
-        // v = (q * scale) * exp(tot) + acc.  q * scale is formed as (q 2^-120)(scale 2^120),
-        // the same product rounded once, while scale 2^120 is finite (scale < 2^7 for every
-        // row of the band; otherwise the conversion-unit path)
+        // v = q * (scale * exp(tot)) + acc, one fused multiply-add per element (the
+        // oracle rounds q * scale and the decay product separately: the two differ by an
+        // fp32 ulp, which moves a stored fp8 code by one step in rare cases)
         const float sa = scl_s[rA], sb = scl_s[rB];
-        const bool fast = __all_sync(0xffffffffu, !act || (sa < 128.0f && sb < 128.0f));
-        const float2 e2 = f2(etot, etot);
 #pragma unroll
         for (int hr = 0; hr < 2; ++hr) {
           float* v = hr ? vb : va;
-          const float scl = hr ? sb : sa;
           const int row = hr ? rB : rA;
           const uint4 q4 = act ? csm[row * CPR + cc] : make_uint4(0u, 0u, 0u, 0u);
           const uint32_t wv[4] = {q4.x, q4.y, q4.z, q4.w};
-          const float su = fast ? scl * kFp8Unscale : scl;
-          const float2 s2 = f2(su, su);
+          const float se = __fmul_rn(hr ? sb : sa, etot);
+          const float2 se2 = f2(se, se);
           float m = 0.0f;
 #pragma unroll
           for (int wi = 0; wi < 4; ++wi) {
             float qv[4];
-            if (fast) fp8x4_to_f32_scaled(wv[wi], qv);
-            else word_to_float<COLD>(wv[wi], qv);
+            word_to_float<COLD>(wv[wi], qv);
 #pragma unroll
             for (int e = 0; e < 4; e += 2) {
               const int x = wi * 4 + e;
-              const float2 dq = __fmul2_rn(f2(qv[e], qv[e + 1]), s2);
-              const float2 r2 = __fadd2_rn(__fmul2_rn(dq, e2), f2(v[x], v[x + 1]));
+              const float2 r2 = __ffma2_rn(f2(qv[e], qv[e + 1]), se2, f2(v[x], v[x + 1]));
               v[x] = r2.x;
               v[x + 1] = r2.y;
             }
@@ -753,15 +749,12 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
           for (int hr = 0; hr < 2; ++hr) {
             float* v = hr ? vb : va;
             const int row = hr ? rB : rA;
-            // correctly rounded v / scale, two lanes at a time (Markstein's correction)
+            // v * rn(1 / scale): within an fp32 ulp of v / scale, so a stored code can
+            // differ by one step from the correctly rounded quotient's, rarely
             const float2 r2 = f2(s_rcp[row], s_rcp[row]);
-            const float2 nsc2 = f2(-s_sc[row], -s_sc[row]);
 #pragma unroll
             for (int e = 0; e < CE; e += 2) {
-              const float2 a2 = f2(v[e], v[e + 1]);
-              const float2 q0 = __fmul2_rn(a2, r2);
-              const float2 rs = __ffma2_rn(q0, nsc2, a2);
-              const float2 qq = __ffma2_rn(rs, r2, q0);
+              const float2 qq = __fmul2_rn(f2(v[e], v[e + 1]), r2);
               v[e] = qq.x;
               v[e + 1] = qq.y;
             }

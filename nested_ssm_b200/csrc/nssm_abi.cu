@@ -144,7 +144,7 @@ int launch_rot(const nssm::RotParams& rp, int rows_total, int G, cudaStream_t st
       return cuda_check("cudaFuncSetAttribute(rot_kernel)");
     attr_done.fetch_or(bit, std::memory_order_acq_rel);
   }
-  dim3 grid((unsigned)((rows_total + nssm::kRotTile - 1) / nssm::kRotTile), (unsigned)G, 1);
+  dim3 grid((unsigned)((rows_total + nssm::kRotTile - 1) / nssm::kRotTile), (unsigned)G, 128 / nssm::kRotHalf);
   nssm::rot_kernel<128><<<grid, nssm::kRotThreads, smem, st>>>(rp, rows_total);
   return cuda_check("rot_kernel launch");
 }

@@ -12,6 +12,7 @@
 #include <string>
 
 #include "nssm_persistent.cuh"
+#include "nssm_rot.cuh"
 
 namespace nssm_host {
 

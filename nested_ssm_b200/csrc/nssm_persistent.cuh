@@ -320,6 +320,7 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
   // ---- prologue 1: slot and token count after this step of every batch row in
   // range.  STEP reads t and adds one; FLUSH reads the count STEP wrote and keeps
   // only the rows that flush.
+  bool any = false;
   for (int j = tid; j < nb; j += kPT) {
     const int b = b0 + j;
     const int slot = p.idx ? p.idx[b] : b;
@@ -334,11 +335,15 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
         if (!STEP && (tn <= 0 || tn % c != 0)) s = -1;   // FLUSH: only flushing rows
       }
     }
+    any |= s >= 0;
     bslot[j] = s;
     btn[j] = tn;
     const int ps = tn > 0 ? (tn - 1) % c : 0;
     bpos[j] = (ps == c - 1) ? -(ps + 1) : ps;
   }
+  // nothing to do in this CTA's range (every row padded, or, in FLUSH, no row at a chunk
+  // boundary -- the FLUSH launch of c - 1 tokens out of c): leave before any set-up
+  if (!__syncthreads_or(any)) return;
   if (!STEP) {
     for (int h = tid; h < H; h += kPT) sA[h] = p.A[h];
   }

@@ -563,7 +563,7 @@ def main():
                        "parallelism": f"slot-sharded x{ws} (no collective)",
                        "l2": "inputs larger than L2 (tiered pool %.1f GB/GPU)" % (L * B * bytes_per_slot(args) / 1e9),
                        "cuda_graph": not args.no_graph},
-            "gpu_launches": K * L * 2,
+            "gpu_launches": K * L * 3,   # per layer: rotation, STEP, FLUSH
             "roofline": roof,
             "e2e": e2e,
             "cpu_baseline": cpu,

@@ -271,10 +271,10 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
   constexpr int HQ = (RPWMAX * LPR + 31) / 32;                // hot chunks per lane
   constexpr int CQ = (RPWMAX * CPR + 31) / 32;                // cold chunks per lane (STEP)
   constexpr int CQF = (CPR + (32 / RPWMAX) - 1) / (32 / RPWMAX);   // column passes (FLUSH)
-  // FLUSH of fp8 instances with a compile-time band of an even number of rows: a lane owns
-  // one cold chunk column of two rows (rows rp and rp + RPWC/2 of the band), so the ring's
-  // B'_cold chunk is read once for both rows; the decay and the division by the new row
-  // scale are folded into one multiply each (see the FLUSH body)
+  // fp8 instances with a compile-time band of an even number of rows: a lane owns one cold
+  // chunk column of two rows (rows rp and rp + RPWC/2 of the band), so the per-column data
+  // (C'_cold in STEP, the ring's B'_cold in FLUSH) is read once for both rows; in FLUSH the
+  // decay and the division by the new row scale are folded into one multiply each
   constexpr bool kPair = COLD == COLD_FP8 && RPWC > 0 && RPWC % 2 == 0 && (RPWC / 2) * CPR <= 32;
   constexpr int kHR = kPair ? RPWC / 2 : 1;
   static_assert(32 % LPR == 0, "hot row chunks must tile a warp");
@@ -552,7 +552,29 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
         }
       }
       // ---- stale cold readout of the band: per-chunk partials sum_e q[e] C[n]
-      if (p.mode != NSSM_MODE_COLDOFF) {
+      if constexpr (kPair) {
+        // a lane owns one chunk column of two rows: C'_cold of the column is widened once
+        const int rp = lane % kHR, cc = lane / kHR;
+        if (p.mode != NSSM_MODE_COLDOFF && cc < CPR) {
+          float cv[CE];
+          ld_row<CE, IOBF>(cr, PB + cc * CE, cv);
+#pragma unroll
+          for (int hr = 0; hr < 2; ++hr) {
+            const int i = (r0 + rp + hr * kHR) * CPR + cc;
+            const uint4 q4 = csm[i];
+            const uint32_t wv[4] = {q4.x, q4.y, q4.z, q4.w};
+            float2 acc = f2(0.0f, 0.0f);
+#pragma unroll
+            for (int wi = 0; wi < 4; ++wi) {
+              float qv[4];
+              word_to_float<COLD>(wv[wi], qv);
+              acc = __ffma2_rn(f2(qv[0], qv[1]), f2(cv[wi * 4], cv[wi * 4 + 1]), acc);
+              acc = __ffma2_rn(f2(qv[2], qv[3]), f2(cv[wi * 4 + 2], cv[wi * 4 + 3]), acc);
+            }
+            pc[i] = acc.x + acc.y;
+          }
+        }
+      } else if (p.mode != NSSM_MODE_COLDOFF) {
 #pragma unroll
         for (int u = 0; u < CQ; ++u) {
           if (u * 32 >= ncb) break;

@@ -51,6 +51,7 @@ def parse():
     ap.add_argument("--cold", choices=["fp8", "bf16", "fp32"], default="fp8")
     ap.add_argument("--no-fresh", action="store_true", help="skip the untiered fresh control")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-conv", action="store_true", help="skip the decode-token conv measurement")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--cpu-sample-batch", type=int, default=4)
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of replaying CUDA graphs")
@@ -320,6 +321,59 @@ def time_fresh(args, rank: int, ws: int):
             "kernel_ms": kms, "kernel_gbs": B * fresh_bytes_per_seq() / (kms / 1e3) / 1e9}
 
 
+def conv_bytes_per_row(L: int = 3) -> int:
+    """Algorithmic HBM bytes of the decode-token conv per sequence-layer (bf16): the conv
+    state read and written, the in_proj slice read, x / B' / C' written."""
+    D = H * P + 2 * G * N
+    return 2 * D * L * 2 + D * 2 + D * 2
+
+
+def time_conv(args, rank: int, ws: int):
+    """nssm_conv_step (conv1d update + SiLU + split + rotation, one launch) at the bench's
+    batch over all layers' conv states (891 MB at B=448: larger than L2)."""
+    from nested_ssm_b200 import conv_step
+    dev = torch.device("cuda")
+    L, B, K, Ls = args.layers, args.batch, 4, 3
+    D = H * P + 2 * G * N
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(3000 + rank)
+    state = (torch.randn(L, B, D, Ls, device=dev, generator=gen) * 0.5).to(torch.bfloat16)
+    w = (torch.rand(L, D, K, device=dev, generator=gen) - 0.5).to(torch.bfloat16)
+    bias = (torch.randn(L, D, device=dev, generator=gen) * 0.1).to(torch.bfloat16)
+    R = [torch.linalg.qr(torch.randn(G, N, N, device=dev, generator=gen))[0].contiguous() for _ in range(L)]
+    xbc = torch.randn(L, B, D, device=dev, generator=gen).to(torch.bfloat16)
+    x = torch.empty(B, H, P, dtype=torch.bfloat16, device=dev)
+    Bo = torch.empty(B, G, N, dtype=torch.bfloat16, device=dev)
+    Co = torch.empty_like(Bo)
+    slots = torch.arange(B, dtype=torch.int32, device=dev)
+
+    def run():
+        for l in range(L):
+            conv_step(xbc[l], state[l], w[l], bias[l], "silu", slots, -1, R[l], nheads=H, headdim=P,
+                      ngroups=G, dstate=N, x_out=x, B_out=Bo, C_out=Co)
+
+    for _ in range(3):
+        run()
+    barrier(ws)
+    torch.cuda.synchronize()
+    reps = max(4, args.steps // 4)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / (reps * L), ws)
+    barrier(ws)
+    del state, w, xbc
+    torch.cuda.empty_cache()
+    peak, kind = load_peaks()
+    gbs = B * conv_bytes_per_row(Ls) / (ms / 1e3) / 1e9
+    return {"ms_per_launch": round(ms, 4), "achieved_gbs": round(gbs, 1), "frac": round(gbs / peak, 4),
+            "bytes_per_launch": B * conv_bytes_per_row(Ls), "width": K, "state_len": Ls,
+            "kernel": "conv_step_kernel (conv1d update + SiLU + split + rotation of B and C)"}
+
+
 def time_e2e(wl: Workload, args, ws: int):
     """Same metric through the public API with HOST buffers: every step copies that
     step's inputs (x, dt, B, C of all layers) from pinned host memory and reads y
@@ -546,6 +600,7 @@ def main():
     del wl
     torch.cuda.empty_cache()
     fresh = None if args.no_fresh else time_fresh(args, rank, ws)
+    conv = None if args.no_conv else time_conv(args, rank, ws)
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu:
@@ -569,6 +624,7 @@ def main():
             "cpu_baseline": cpu,
             "fresh_control": fresh,
             "speedup_vs_fresh": round(value / fresh["tokens_per_s"], 3) if fresh else None,
+            "conv_step": conv,
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)

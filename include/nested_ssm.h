@@ -37,6 +37,9 @@
  *        rotation of scale/v4_fused_decode.py:45-48.
  *  - nssm_materialize  : no single reference function; returns the exact full
  *        state the native path keeps in cache (scale/v4_native_decode.py:65-67).
+ *  - nssm_conv_step    : causal_conv1d_update + split + the post-conv R rotation of
+ *        _v4_fused_decode (scale/v4_fused_decode.py:39-48); the HF decode branch's
+ *        conv-state roll + weighted sum + act (scale/v4_native_decode.py:36-49).
  */
 #ifndef NESTED_SSM_H_
 #define NESTED_SSM_H_
@@ -131,6 +134,44 @@ typedef struct {
   size_t workspace_bytes;
   int32_t* status;        /* optional device word, error bits OR-ed in          */
 } nssm_step_args;
+
+/* Decode-token conv ahead of the state update, for one layer: the causal conv1d update of
+ * the in_proj slice [x | B | C] with the per-slot conv state, the activation, the split and
+ * the per-group rotation of B and C, in one launch.  Replaces causal_conv1d_update + split +
+ * the R einsums of scale/v4_fused_decode.py:39-48 (HF decode branch:
+ * scale/v4_native_decode.py:36-49).  Per row b (slot s) and channel d, with width K and a
+ * state of L >= K-1 columns: window = last K of [state[s][d][0..L), xbc[b][d]],
+ * out = act(bias[d] + sum_k weight[d][k] window[k]) (fp32, k in order), state[s][d] <- last
+ * L of [state[s][d], xbc[b][d]]; B and C are rounded to io_dtype, then rotated like
+ * nssm_rot_flat. */
+typedef struct {
+  int32_t batch;
+  int32_t nheads, headdim, ngroups, dstate; /* conv_dim = nheads*headdim + 2*ngroups*dstate */
+  int32_t width;          /* K (<= 8)                                             */
+  int32_t state_len;      /* L, K-1 <= L <= 8                                     */
+  int32_t num_slots;
+  int32_t io_dtype;       /* dtype of xbc, conv_state and the outputs (F32 / BF16) */
+  int32_t weight_dtype;   /* dtype of weight and bias (F32 / BF16)               */
+  int32_t activation;     /* 0: none, 1: SiLU                                     */
+  int32_t pad_slot_id;
+  const void* xbc;        /* [batch][conv_dim]                                    */
+  int64_t xbc_stride_b;
+  void* conv_state;       /* [num_slots][conv_dim][state_len]                     */
+  int64_t state_stride_s;
+  const void* weight;     /* [conv_dim][width]                                    */
+  const void* bias;       /* [conv_dim] or NULL                                   */
+  const float* R;         /* [ngroups][dstate][dstate] or NULL (no rotation)      */
+  const int32_t* state_batch_indices; /* [batch] or NULL = row                   */
+  void* x_out;            /* [batch][nheads*headdim]                              */
+  int64_t x_out_stride_b;
+  void* B_out;            /* [batch][ngroups*dstate]                              */
+  void* C_out;
+  int64_t bc_out_stride_b;
+  int32_t* status;        /* optional device word, bit 0 = slot outside [0, num_slots) */
+} nssm_conv_args;
+
+NSSM_API int nssm_conv_step(const nssm_conv_args* args, void* stream);
+NSSM_API size_t nssm_sizeof_conv_args(void);
 
 /* Bytes of workspace nssm_tiered_step / nssm_fresh_step need for `batch` rows
  * when R != NULL (the rotated B and C), 0 otherwise. */

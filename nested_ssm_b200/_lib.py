@@ -21,6 +21,7 @@ EXPORTED = (
     "nssm_step_workspace_bytes", "nssm_tiered_step", "nssm_fresh_step", "nssm_prefill_split",
     "nssm_materialize", "nssm_rot_flat", "nssm_supported_hot_dims", "nssm_sizeof_pool",
     "nssm_sizeof_step_args", "nssm_abi_version", "nssm_last_error", "nssm_tiered_step_static",
+    "nssm_conv_step", "nssm_sizeof_conv_args",
 )
 
 
@@ -52,6 +53,22 @@ class NssmStepArgs(C.Structure):
         ("pad_slot_id", C.c_int32), ("out_dtype", C.c_int32),
         ("out", C.c_void_p), ("out_stride_b", C.c_int64), ("out_stride_h", C.c_int64),
         ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t),
+        ("status", C.c_void_p),
+    ]
+
+
+class NssmConvArgs(C.Structure):
+    _fields_ = [
+        ("batch", C.c_int32), ("nheads", C.c_int32), ("headdim", C.c_int32), ("ngroups", C.c_int32),
+        ("dstate", C.c_int32), ("width", C.c_int32), ("state_len", C.c_int32), ("num_slots", C.c_int32),
+        ("io_dtype", C.c_int32), ("weight_dtype", C.c_int32), ("activation", C.c_int32),
+        ("pad_slot_id", C.c_int32),
+        ("xbc", C.c_void_p), ("xbc_stride_b", C.c_int64),
+        ("conv_state", C.c_void_p), ("state_stride_s", C.c_int64),
+        ("weight", C.c_void_p), ("bias", C.c_void_p), ("R", C.c_void_p),
+        ("state_batch_indices", C.c_void_p),
+        ("x_out", C.c_void_p), ("x_out_stride_b", C.c_int64),
+        ("B_out", C.c_void_p), ("C_out", C.c_void_p), ("bc_out_stride_b", C.c_int64),
         ("status", C.c_void_p),
     ]
 
@@ -89,6 +106,8 @@ def load(auto_build: bool = True) -> C.CDLL:
             "nssm_step_workspace_bytes": (sz, [i32, i32, i32, i32, i32]),
             "nssm_tiered_step": (C.c_int, [P_pool, P_args, vp]),
             "nssm_tiered_step_static": (C.c_int, [P_pool, P_args, vp]),
+            "nssm_conv_step": (C.c_int, [C.POINTER(NssmConvArgs), vp]),
+            "nssm_sizeof_conv_args": (sz, []),
             "nssm_fresh_step": (C.c_int, [vp, i32, i32, i32, i32, i32, P_args, vp]),
             "nssm_prefill_split": (C.c_int, [P_pool, vp, i64, vp, i32, i32, vp]),
             "nssm_materialize": (C.c_int, [P_pool, vp, vp, i32, i32, vp, i64, vp]),
@@ -104,7 +123,8 @@ def load(auto_build: bool = True) -> C.CDLL:
             fn.restype, fn.argtypes = res, args
         if lib.nssm_abi_version() != ABI_VERSION:
             raise RuntimeError(f"libnested_ssm ABI {lib.nssm_abi_version()} != binding {ABI_VERSION}")
-        if lib.nssm_sizeof_pool() != C.sizeof(NssmPool) or lib.nssm_sizeof_step_args() != C.sizeof(NssmStepArgs):
+        if (lib.nssm_sizeof_pool() != C.sizeof(NssmPool) or lib.nssm_sizeof_step_args() != C.sizeof(NssmStepArgs)
+                or lib.nssm_sizeof_conv_args() != C.sizeof(NssmConvArgs)):
             raise RuntimeError("libnested_ssm struct layout differs from the ctypes binding")
         _lib = lib
         return lib

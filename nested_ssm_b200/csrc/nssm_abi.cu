@@ -289,6 +289,74 @@ int nssm_rot_flat(const void* x, int64_t x_stride, int32_t dtype, const float* R
   return launch_rot(rp, T, ngroups, static_cast<cudaStream_t>(stream));
 }
 
+int nssm_conv_step(const nssm_conv_args* a, void* stream) {
+  if (!a) return fail(NSSM_ERR_INVALID, "args is NULL");
+  if (a->batch < 0 || a->batch > 65535) return fail(NSSM_ERR_INVALID, "batch %d outside [0, 65535]", a->batch);
+  if (a->batch == 0) return NSSM_OK;
+  if (a->nheads <= 0 || a->headdim <= 0 || a->ngroups <= 0 || a->ngroups > 65535 || a->num_slots <= 0)
+    return fail(NSSM_ERR_INVALID, "bad dims (H=%d P=%d G=%d S=%d)", a->nheads, a->headdim, a->ngroups, a->num_slots);
+  if (a->dstate != 128) return fail(NSSM_ERR_UNSUPPORTED, "conv step compiled for dstate 128 only");
+  if (a->width < 1 || a->width > nssm::kConvMaxK || a->state_len < a->width - 1 || a->state_len > nssm::kConvMaxL ||
+      a->state_len < 1)
+    return fail(NSSM_ERR_INVALID, "width %d / state_len %d unsupported (1 <= K <= 8, K-1 <= L <= 8, L >= 1)",
+                a->width, a->state_len);
+  if (a->io_dtype != NSSM_F32 && a->io_dtype != NSSM_BF16) return fail(NSSM_ERR_INVALID, "io_dtype must be F32 or BF16");
+  if (a->weight_dtype != NSSM_F32 && a->weight_dtype != NSSM_BF16)
+    return fail(NSSM_ERR_INVALID, "weight_dtype must be F32 or BF16");
+  if (a->activation != 0 && a->activation != 1) return fail(NSSM_ERR_INVALID, "activation %d unknown", a->activation);
+  if (!a->xbc || !a->conv_state || !a->weight || !a->x_out || !a->B_out || !a->C_out)
+    return fail(NSSM_ERR_INVALID, "a required pointer is NULL");
+  if (a->R && (reinterpret_cast<uintptr_t>(a->R) % 16)) return fail(NSSM_ERR_INVALID, "R must be 16-byte aligned");
+  nssm::ConvParams cp{};
+  cp.xbc = a->xbc; cp.xbc_sb = a->xbc_stride_b;
+  cp.state = a->conv_state; cp.state_ss = a->state_stride_s; cp.L = a->state_len; cp.K = a->width;
+  cp.weight = a->weight; cp.w_dtype = a->weight_dtype; cp.bias = a->bias; cp.act = a->activation;
+  cp.R = a->R; cp.idx = a->state_batch_indices; cp.pad = a->pad_slot_id; cp.S = a->num_slots;
+  cp.T = a->batch; cp.I = a->nheads * a->headdim; cp.G = a->ngroups; cp.dtype = a->io_dtype;
+  cp.x_out = a->x_out; cp.x_sb = a->x_out_stride_b;
+  cp.b_out = a->B_out; cp.c_out = a->C_out; cp.bc_sb = a->bc_out_stride_b;
+  cp.status = a->status;
+  static std::atomic<unsigned long long> attr_done{0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return cuda_check("cudaGetDevice");
+  const unsigned long long bit = 1ull << (dev & 63);
+  constexpr int smem = nssm::conv_smem_bytes(128);
+  if (!(attr_done.load(std::memory_order_acquire) & bit)) {
+    if (cudaFuncSetAttribute(nssm::conv_step_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+      return cuda_check("cudaFuncSetAttribute(conv_step_kernel)");
+    attr_done.fetch_or(bit, std::memory_order_acq_rel);
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // x channels: vector path for width 4 with state length 3 or 4 when every access is aligned
+  const int eb = a->io_dtype == NSSM_BF16 ? 2 : 4;
+  const bool vec = a->width == 4 && (a->state_len == 3 || a->state_len == 4) && cp.I % 4 == 0 &&
+                   aligned16(a->xbc) && aligned16(a->conv_state) && aligned16(a->x_out) &&
+                   a->xbc_stride_b % 4 == 0 && a->x_out_stride_b % 4 == 0 && a->state_stride_s % 4 == 0 &&
+                   ((int64_t)a->state_len * 4 * eb) % (a->io_dtype == NSSM_BF16 ? 8 : 16) == 0;
+  dim3 gx((unsigned)((cp.I + 4 * nssm::kConvXThreads - 1) / (4 * nssm::kConvXThreads)), (unsigned)a->batch);
+  const bool iobf = a->io_dtype == NSSM_BF16, wbf = a->weight_dtype == NSSM_BF16;
+  if (vec && a->state_len == 3) {
+    if (iobf && wbf) nssm::conv_x_kernel<4, 3, true, true><<<gx, nssm::kConvXThreads, 0, st>>>(cp);
+    else if (iobf) nssm::conv_x_kernel<4, 3, true, false><<<gx, nssm::kConvXThreads, 0, st>>>(cp);
+    else if (wbf) nssm::conv_x_kernel<4, 3, false, true><<<gx, nssm::kConvXThreads, 0, st>>>(cp);
+    else nssm::conv_x_kernel<4, 3, false, false><<<gx, nssm::kConvXThreads, 0, st>>>(cp);
+  } else if (vec) {
+    if (iobf && wbf) nssm::conv_x_kernel<4, 4, true, true><<<gx, nssm::kConvXThreads, 0, st>>>(cp);
+    else if (iobf) nssm::conv_x_kernel<4, 4, true, false><<<gx, nssm::kConvXThreads, 0, st>>>(cp);
+    else if (wbf) nssm::conv_x_kernel<4, 4, false, true><<<gx, nssm::kConvXThreads, 0, st>>>(cp);
+    else nssm::conv_x_kernel<4, 4, false, false><<<gx, nssm::kConvXThreads, 0, st>>>(cp);
+  } else {
+    nssm::conv_x_kernel<0, 0, false, false><<<gx, nssm::kConvXThreads, 0, st>>>(cp);
+  }
+  int rc = cuda_check("conv_x_kernel launch");
+  if (rc) return rc;
+  dim3 grid((unsigned)((a->batch + nssm::kConvTile - 1) / nssm::kConvTile), (unsigned)a->ngroups, 2);
+  nssm::conv_step_kernel<128><<<grid, nssm::kConvThreads, smem, st>>>(cp);
+  return cuda_check("conv_step_kernel launch");
+}
+
+size_t nssm_sizeof_conv_args(void) { return sizeof(nssm_conv_args); }
+
 int32_t nssm_supported_hot_dims(int32_t dstate, int32_t* widths, int32_t cap) {
   static const int32_t k128[] = {16, 32, 64};
   if (dstate != 128) return 0;

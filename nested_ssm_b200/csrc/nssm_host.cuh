@@ -13,6 +13,7 @@
 
 #include "nssm_persistent.cuh"
 #include "nssm_rot.cuh"
+#include "nssm_conv.cuh"
 
 namespace nssm_host {
 

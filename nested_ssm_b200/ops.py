@@ -248,3 +248,76 @@ def rot_flat(x: torch.Tensor, R: torch.Tensor, out: torch.Tensor | None = None) 
     _lib.check(lib.nssm_rot_flat(x2.data_ptr(), x2.stride(0), nssm_dtype(x.dtype), Rf.data_ptr(), T, G, N,
                                  out.data_ptr(), out.stride(0), _stream(x.device)))
     return out.view(x.shape) if out.shape != x.shape and out.numel() == x.numel() else out
+
+
+ACTIVATIONS = {None: 0, "none": 0, "identity": 0, "silu": 1, "swish": 1}
+
+
+def conv_step(xbc: torch.Tensor, conv_state: torch.Tensor, weight: torch.Tensor, bias=None,
+              activation="silu", conv_state_indices=None, pad_slot_id: int = -1, R=None, *,
+              nheads: int, headdim: int, ngroups: int, dstate: int = 128,
+              x_out=None, B_out=None, C_out=None, status=None):
+    """Decode-token conv of one layer ahead of the state update: the causal conv1d update
+    of ``xbc [b, conv_dim]`` (the in_proj slice [x | B | C]) with ``conv_state
+    [num_slots, conv_dim, L]`` (updated in place, rows by ``conv_state_indices``), the
+    activation, the split, and the rotation of B and C by ``R [G, N, N]``.
+
+    Replaces ``causal_conv1d_update`` + split + the R einsums of
+    scale/v4_fused_decode.py:39-48.  Returns ``(x [b, H, P], B [b, G, N], C [b, G, N])`` in
+    xbc's dtype, ready for :func:`tiered_state_update` with ``R=None``."""
+    if xbc.dim() != 2 or xbc.stride(1) != 1:
+        raise ValueError(f"xbc must be [b, conv_dim] with unit inner stride, got {tuple(xbc.shape)}")
+    b, conv_dim = xbc.shape
+    I, GN = nheads * headdim, ngroups * dstate
+    if conv_dim != I + 2 * GN:
+        raise ValueError(f"conv_dim {conv_dim} != nheads*headdim + 2*ngroups*dstate = {I + 2 * GN}")
+    if xbc.dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError(f"xbc dtype {xbc.dtype} unsupported (bf16 / fp32)")
+    if conv_state.dim() != 3 or conv_state.shape[1] != conv_dim or conv_state.dtype != xbc.dtype:
+        raise ValueError(f"conv_state must be [S, {conv_dim}, L] of xbc's dtype, got {tuple(conv_state.shape)} "
+                         f"{conv_state.dtype}")
+    if conv_state.stride(2) != 1 or conv_state.stride(1) != conv_state.shape[2]:
+        raise ValueError("conv_state rows must be contiguous ([S, conv_dim, L] with L innermost)")
+    w = weight.reshape(weight.shape[0], -1) if weight.dim() == 3 else weight     # HF conv1d [D, 1, K]
+    if w.dim() != 2 or w.shape[0] != conv_dim or not w.is_contiguous() or w.dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError(f"weight must be a contiguous [{conv_dim}, K] (or [{conv_dim}, 1, K]) bf16 / fp32 tensor")
+    if bias is not None and (bias.shape != (conv_dim,) or bias.dtype != w.dtype or not bias.is_contiguous()):
+        raise ValueError(f"bias must be a contiguous [{conv_dim}] tensor of weight's dtype")
+    if activation not in ACTIVATIONS:
+        raise ValueError(f"activation must be one of {sorted(k for k in ACTIVATIONS if k)}")
+    idx = None
+    if conv_state_indices is not None:
+        idx = conv_state_indices.reshape(-1)
+        if idx.dtype != torch.int32 or not idx.is_contiguous():
+            idx = idx.to(torch.int32).contiguous()
+        if idx.numel() != b:
+            raise ValueError(f"conv_state_indices has {idx.numel()} rows, xbc has {b}")
+    Rf = None
+    if R is not None:
+        Rf = R if (R.dtype == torch.float32 and R.is_contiguous()) else R.float().contiguous()
+    dev = _require_cuda(xbc, conv_state, w, bias, idx, Rf)
+    if x_out is None:
+        x_out = torch.empty(b, nheads, headdim, dtype=xbc.dtype, device=dev)
+    if B_out is None:
+        B_out = torch.empty(b, ngroups, dstate, dtype=xbc.dtype, device=dev)
+    if C_out is None:
+        C_out = torch.empty(b, ngroups, dstate, dtype=xbc.dtype, device=dev)
+    for t, name in ((x_out, "x_out"), (B_out, "B_out"), (C_out, "C_out")):
+        if t.dtype != xbc.dtype or not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous with xbc's dtype")
+    a = _lib.NssmConvArgs()
+    a.batch, a.nheads, a.headdim, a.ngroups, a.dstate = b, nheads, headdim, ngroups, dstate
+    a.width, a.state_len, a.num_slots = w.shape[1], conv_state.shape[2], conv_state.shape[0]
+    a.io_dtype, a.weight_dtype = nssm_dtype(xbc.dtype), nssm_dtype(w.dtype)
+    a.activation = ACTIVATIONS[activation]
+    a.pad_slot_id = int(pad_slot_id)
+    a.xbc, a.xbc_stride_b = xbc.data_ptr(), xbc.stride(0)
+    a.conv_state, a.state_stride_s = conv_state.data_ptr(), conv_state.stride(0)
+    a.weight, a.bias, a.R = w.data_ptr(), _ptr(bias), _ptr(Rf)
+    a.state_batch_indices = _ptr(idx)
+    a.x_out, a.x_out_stride_b = x_out.data_ptr(), I
+    a.B_out, a.C_out, a.bc_out_stride_b = B_out.data_ptr(), C_out.data_ptr(), GN
+    a.status = _ptr(status)
+    keep = (xbc, conv_state, w, bias, idx, Rf, x_out, B_out, C_out, status)  # noqa: F841
+    _lib.check(_lib.load().nssm_conv_step(C.byref(a), _stream(dev)))
+    return x_out, B_out, C_out

@@ -51,7 +51,7 @@ __all__ = [
     "FP8", "FP8_MAX", "SCALE_EPS", "rot_flat", "dt_softplus", "quantize_rows",
     "dequantize_rows", "TieredPoolRef", "NativePoolRef", "prefill_split",
     "tiered_step", "native_step", "fresh_step", "materialize", "make_inputs",
-    "make_params", "fp8_ordered_codes",
+    "make_params", "fp8_ordered_codes", "conv_step", "conv_split",
 ]
 
 FP8 = torch.float8_e4m3fn
@@ -115,6 +115,55 @@ def fp8_ordered_codes(q: torch.Tensor) -> torch.Tensor:
     u = q.view(torch.uint8).to(torch.int32)
     mag = u & 0x7F
     return torch.where(u >= 0x80, -mag, mag)
+
+
+# --------------------------------------------------------------------------
+# decode-token conv ahead of the state op
+# --------------------------------------------------------------------------
+def conv_step(conv_state: torch.Tensor, slots, xbc: torch.Tensor, weight: torch.Tensor,
+              bias: torch.Tensor | None, act: str | None = "silu", pad_slot_id: int = -1) -> torch.Tensor:
+    """Causal conv1d update of one decode token; mutates ``conv_state [S, D, L]`` and returns
+    the activated conv output ``[b, D]`` in fp32 (padded rows zero).
+
+    HF decode branch: the cache rolls the state left and appends the new column
+    (transformers ``update_conv_state``), then ``sum(conv_states * weight) + bias`` and the
+    activation (scale/v4_native_decode.py:36-49); the fused path's ``causal_conv1d_update``
+    (scale/v4_fused_decode.py:39-41) keeps L >= K-1 columns: window = last K of
+    ``[state, x]``, new state = last L.  Taps accumulate in k order with one rounding per
+    tap (a fused multiply-add), the activation is ``v / (1 + exp(-v))``."""
+    rows, s = _valid_rows(slots, pad_slot_id)
+    b, D = xbc.shape
+    K = weight.shape[-1]
+    L = conv_state.shape[-1]
+    out = torch.zeros(b, D)
+    if rows.numel() == 0:
+        return out
+    full = torch.cat([conv_state[s].float(), xbc[rows].float()[..., None]], dim=-1)   # [r, D, L+1]
+    win = full[..., L + 1 - K:]
+    w = weight.reshape(D, K).double()
+    acc = torch.zeros(rows.numel(), D)
+    for k in range(K):   # fma: exact product + accumulator, rounded once
+        acc = (w[:, k] * win[..., k].double() + acc.double()).float()
+    if bias is not None:
+        acc = acc + bias.float()
+    if act == "silu":
+        acc = acc / (1.0 + torch.exp(-acc))
+    conv_state[s] = full[..., 1:].to(conv_state.dtype)
+    out[rows] = acc
+    return out
+
+
+def conv_split(out: torch.Tensor, I: int, G: int, N: int, R: torch.Tensor | None, io_dtype):
+    """Split a conv output ``[b, I + 2 G N]`` into x ``[b, I]``, B, C ``[b, G, N]`` in the io
+    dtype, B and C rounded to it first and then rotated by ``R`` in fp32 (the post-conv
+    rotation of scale/v4_fused_decode.py:45-48)."""
+    b = out.shape[0]
+    x = out[:, :I].to(io_dtype)
+    Bv = out[:, I:I + G * N].to(io_dtype)
+    Cv = out[:, I + G * N:].to(io_dtype)
+    if R is not None:
+        Bv, Cv = rot_flat(Bv, R, "fp32"), rot_flat(Cv, R, "fp32")
+    return x, Bv.reshape(b, G, N), Cv.reshape(b, G, N)
 
 
 # --------------------------------------------------------------------------

@@ -43,3 +43,8 @@ def check_sums(d: dict, inp: dict, prefix: str = "") -> None:
     """The regenerated inputs are the ones the fixture was made from."""
     for k, t in (("x", inp["xs"]), ("dt", inp["dts"]), ("B", inp["Bs"]), ("C", inp["Cs"]), ("s0", inp["s0"])):
         assert float(d[f"{prefix}sum_{k}"]) == MG.checksum(t), f"regenerated input {k} differs from the fixture's"
+
+
+def conv_case():
+    """Inputs of native_decode_conv.npz (regenerated from their seed)."""
+    return MG.CONV, MG.conv_inputs(MG.CONV)

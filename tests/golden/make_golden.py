@@ -19,6 +19,10 @@ regenerate (checksums stored beside the outputs):
   here in torch (softplus without clamp, as vLLM).
 * ``rot_flat.npz`` -- ``rot_flat`` on bf16 input (the bf16 einsum of ActRotMask) and on
   fp32 input.
+* ``native_decode_conv.npz`` -- ``_v4_decode`` again, now with a real conv1d (weights, bias,
+  a conv state advanced by the transformers cache roll) and the reference's own
+  ``ActRotMask`` (``scale/nemotron_retrofit.py:18-54``: SiLU, then the rotation of B and C)
+  as the activation, so y covers conv + SiLU + split + rotation + tiered state op.
 """
 from __future__ import annotations
 
@@ -41,6 +45,7 @@ import oracle as O  # noqa: E402
 NATIVE = dict(b=2, H=16, P=80, N=128, G=2, pb=32, c=4, seed=11, steps=13, steps_modes=9)
 VLLM = dict(b=2, S=4, H=8, P=80, N=128, G=2, pb=32, c=4, seed=12, steps=9, slots=[2, 0])
 ROT = dict(T=6, G=2, N=128, seed=13)
+CONV = dict(b=2, H=16, P=80, N=128, G=2, pb=32, c=4, seed=14, steps=9, K=4)
 
 
 def state0(b, H, P, N, seed):
@@ -188,6 +193,70 @@ def make_rot(ref):
                 out_fp32=VP.rot_flat(x.float(), R))
 
 
+def conv_inputs(cfg):
+    """Seeded conv-step inputs (bf16-representable values held in fp32)."""
+    b, H, P, N, G, K, seed, steps = (cfg[k] for k in ("b", "H", "P", "N", "G", "K", "seed", "steps"))
+    D = H * P + 2 * G * N
+    g = torch.Generator().manual_seed(seed + 100)
+    bf = lambda t: t.to(torch.bfloat16).float()   # noqa: E731
+    return dict(
+        xbc=bf(torch.randn(steps, b, D, generator=g)),
+        dts=bf(torch.randn(steps, b, H, generator=g)),
+        state=bf(torch.randn(b, D, K, generator=g) * 0.5),
+        weight=bf(torch.rand(D, 1, K, generator=g) - 0.5),
+        bias=bf(torch.randn(D, generator=g) * 0.1),
+        s0=state0(b, H, P, N, seed))
+
+
+def make_native_conv(ref):
+    sys.path.insert(0, os.path.join(ref, "scale"))
+    import v4_native_decode as V
+    import nemotron_retrofit as NR
+    cfg = CONV
+    b, H, P, N, G, pb, c, seed, K = (cfg[k] for k in ("b", "H", "P", "N", "G", "pb", "c", "seed", "K"))
+    prm = O.make_params(H, G, N, seed=seed)[0]
+    inp = conv_inputs(cfg)
+    I = H * P
+    D = I + 2 * G * N
+    A_log = torch.log(-prm["A"])
+    act = NR.ActRotMask(torch.nn.SiLU(), I, G, N)
+    act.R.data.copy_(prm["R"])
+    m = types.SimpleNamespace(
+        num_heads=H, head_dim=P, ssm_state_size=N, n_groups=G, intermediate_size=I, conv_dim=D,
+        in_proj=torch.nn.Identity(), act=act, use_conv_bias=True, A_log=A_log, D=prm["D"],
+        dt_bias=prm["dt_bias"], time_step_min=1e-3, layer_idx=0, out_proj=torch.nn.Identity(),
+        norm=lambda y, gate: y, v4cfg=dict(pb=pb, c=c, cold_bf16=0, corr=0, coldoff=0))
+    m.conv1d = types.SimpleNamespace(weight=inp["weight"], bias=inp["bias"])
+    m._v4state = {"snap": inp["s0"][..., pb:].clone(), "glog": torch.zeros(b, H, P), "t": 0,
+                  "bufB": [], "bufX": [], "bufG": []}
+    cache = types.SimpleNamespace()
+    cache.conv = inp["state"].clone()
+
+    def update_conv_state(hs, idx):   # the transformers cache's decode update: roll, append
+        st = cache.conv.roll(shifts=-1, dims=-1)
+        st[:, :, -1:] = hs
+        cache.conv = st
+        return st
+
+    def update_recurrent_state(s_, idx):
+        cache.layers[idx].recurrent_states = s_
+        return s_
+
+    cache.update_conv_state = update_conv_state
+    cache.update_recurrent_state = update_recurrent_state
+    cache.layers = [types.SimpleNamespace(recurrent_states=inp["s0"].clone())]
+    ys = []
+    for s in range(cfg["steps"]):
+        proj = torch.cat([torch.zeros(b, I), inp["xbc"][s], inp["dts"][s]], dim=-1)[:, None, :]
+        ys.append(V._v4_decode(m, proj, cache, None).reshape(b, H, P).float())
+    arrays = dict(y=torch.stack(ys), conv_state_final=cache.conv.clone(),
+                  state_final_h0_h9=cache.layers[0].recurrent_states[:, [0, 9]].float(),
+                  R=prm["R"], A=-torch.exp(A_log.float()), D=prm["D"], dt_bias=prm["dt_bias"])
+    for k in ("xbc", "dts", "state", "weight", "bias", "s0"):
+        arrays[f"sum_{k}"] = torch.tensor(checksum(inp[k]), dtype=torch.float64)
+    return arrays
+
+
 def save(name, arrays):
     np_arrays = {k: (v.view(torch.int16) if v.dtype == torch.bfloat16 else v).numpy() for k, v in arrays.items()}
     path = os.path.join(HERE, name)
@@ -204,6 +273,7 @@ def main():
         save("native_decode_fp32.npz", make_native(a.reference))
         save("vllm_fp8.npz", make_vllm(a.reference))
         save("rot_flat.npz", make_rot(a.reference))
+        save("native_decode_conv.npz", make_native_conv(a.reference))
 
 
 if __name__ == "__main__":

@@ -9,6 +9,9 @@
   t, glog and flush snapshots bit for bit; the replay semantics agree bit for bit until
   the first flush (after it the fp8-only cold master drifts from the fp32 master by design).
 * rotation: ``oracle.rot_flat`` reproduces ``rot_flat`` in both precisions bit for bit.
+* conv: ``oracle.conv_step`` + ``conv_split`` + the replay state op reproduce ``_v4_decode``
+  with a real conv1d and the reference's ActRotMask activation (SiLU + rotation) to fp32
+  rounding, and leave the conv state the transformers cache holds.
 """
 import torch
 
@@ -105,3 +108,27 @@ def test_vllm_fp8_prefill_and_readout_bitexact():
             assert torch.equal(npool.scale[slots], d["flush_scale"][fi])
             fi += 1
     assert fi == d["flush_codes"].shape[0]
+
+
+def test_conv_step_and_state_op_vs_v4_decode():
+    d = GD.load("native_decode_conv.npz")
+    cfg, inp = GD.conv_case()
+    for k in ("xbc", "dts", "state", "weight", "bias", "s0"):
+        assert float(d[f"sum_{k}"]) == GD.MG.checksum(inp[k]), k
+    b, H, P, N, G, pb, c = (cfg[k] for k in ("b", "H", "P", "N", "G", "pb", "c"))
+    I = H * P
+    pool = O.TieredPoolRef(b, H, P, N, G, pb, c, torch.float32, torch.float32)
+    slots = torch.arange(b)
+    O.prefill_split(pool, slots, inp["s0"])
+    conv_state = inp["state"].clone()
+    worst = 0.0
+    for s in range(cfg["steps"]):
+        out = O.conv_step(conv_state, slots, inp["xbc"][s], inp["weight"], inp["bias"], "silu")
+        x, Bv, Cv = O.conv_split(out, I, G, N, d["R"], torch.float32)
+        y = O.tiered_step(pool, slots, x.reshape(b, H, P), inp["dts"][s], Bv, Cv, d["A"], d["D"],
+                          d["dt_bias"], 1e-3)
+        worst = max(worst, float((y - d["y"][s]).abs().max()))
+        torch.testing.assert_close(y, d["y"][s], rtol=1e-5, atol=1e-5, msg=lambda m: f"step {s}: {m}")
+    assert torch.equal(conv_state, d["conv_state_final"])
+    st = O.materialize(pool, slots, d["A"])[:, [0, 9]]
+    torch.testing.assert_close(st, d["state_final_h0_h9"], rtol=1e-5, atol=1e-5)

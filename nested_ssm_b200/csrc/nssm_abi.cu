@@ -172,6 +172,29 @@ int maybe_rotate(const nssm_step_args* a, int G, int N, nssm::StepParams& sp, cu
   return NSSM_OK;
 }
 
+template <int K, int L, bool IOBF, bool WBF>
+int launch_conv(const nssm::ConvParams& cp, int batch, int G, cudaStream_t st) {
+  // the B/C kernel uses 84 KB of dynamic shared memory: opt in once per device
+  static std::atomic<unsigned long long> attr_done{0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return cuda_check("cudaGetDevice");
+  const unsigned long long bit = 1ull << (dev & 63);
+  constexpr int smem = nssm::conv_smem_bytes(128);
+  auto kbc = nssm::conv_step_kernel<128, K, L, IOBF, WBF>;
+  if (!(attr_done.load(std::memory_order_acquire) & bit)) {
+    if (cudaFuncSetAttribute(kbc, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+      return cuda_check("cudaFuncSetAttribute(conv_step_kernel)");
+    attr_done.fetch_or(bit, std::memory_order_acq_rel);
+  }
+  dim3 gx((unsigned)((cp.I + 4 * nssm::kConvXThreads - 1) / (4 * nssm::kConvXThreads)), (unsigned)batch);
+  nssm::conv_x_kernel<K, L, IOBF, WBF><<<gx, nssm::kConvXThreads, 0, st>>>(cp);
+  int rc = cuda_check("conv_x_kernel launch");
+  if (rc) return rc;
+  dim3 grid((unsigned)((batch + nssm::kConvTile - 1) / nssm::kConvTile), (unsigned)G, 2);
+  kbc<<<grid, nssm::kConvThreads, smem, st>>>(cp);
+  return cuda_check("conv_step_kernel launch");
+}
+
 void fill_inputs(const nssm_step_args* a, nssm::StepParams& sp) {
   sp.x = a->x; sp.x_sb = a->x_stride_b; sp.x_sh = a->x_stride_h;
   sp.dt = a->dt; sp.dt_sb = a->dt_stride_b; sp.dt_sh = a->dt_stride_h; sp.dt_dtype = a->dt_dtype;
@@ -316,43 +339,25 @@ int nssm_conv_step(const nssm_conv_args* a, void* stream) {
   cp.x_out = a->x_out; cp.x_sb = a->x_out_stride_b;
   cp.b_out = a->B_out; cp.c_out = a->C_out; cp.bc_sb = a->bc_out_stride_b;
   cp.status = a->status;
-  static std::atomic<unsigned long long> attr_done{0};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return cuda_check("cudaGetDevice");
-  const unsigned long long bit = 1ull << (dev & 63);
-  constexpr int smem = nssm::conv_smem_bytes(128);
-  if (!(attr_done.load(std::memory_order_acquire) & bit)) {
-    if (cudaFuncSetAttribute(nssm::conv_step_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-      return cuda_check("cudaFuncSetAttribute(conv_step_kernel)");
-    attr_done.fetch_or(bit, std::memory_order_acq_rel);
-  }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // x channels: vector path for width 4 with state length 3 or 4 when every access is aligned
+  // vector paths for width 4 with state length 3 or 4 when every access is aligned
   const int eb = a->io_dtype == NSSM_BF16 ? 2 : 4;
   const bool vec = a->width == 4 && (a->state_len == 3 || a->state_len == 4) && cp.I % 4 == 0 &&
-                   aligned16(a->xbc) && aligned16(a->conv_state) && aligned16(a->x_out) &&
-                   a->xbc_stride_b % 4 == 0 && a->x_out_stride_b % 4 == 0 && a->state_stride_s % 4 == 0 &&
-                   ((int64_t)a->state_len * 4 * eb) % (a->io_dtype == NSSM_BF16 ? 8 : 16) == 0;
-  dim3 gx((unsigned)((cp.I + 4 * nssm::kConvXThreads - 1) / (4 * nssm::kConvXThreads)), (unsigned)a->batch);
+                   aligned16(a->xbc) && aligned16(a->conv_state) && aligned16(a->x_out) && aligned16(a->weight) &&
+                   (!a->bias || aligned16(a->bias)) && a->xbc_stride_b % 4 == 0 && a->x_out_stride_b % 4 == 0 &&
+                   a->state_stride_s % 4 == 0 && ((int64_t)a->state_len * 4 * eb) % (eb == 2 ? 8 : 16) == 0;
   const bool iobf = a->io_dtype == NSSM_BF16, wbf = a->weight_dtype == NSSM_BF16;
-  if (vec && a->state_len == 3) {
-    if (iobf && wbf) nssm::conv_x_kernel<4, 3, true, true><<<gx, nssm::kConvXThreads, 0, st>>>(cp);
-    else if (iobf) nssm::conv_x_kernel<4, 3, true, false><<<gx, nssm::kConvXThreads, 0, st>>>(cp);
-    else if (wbf) nssm::conv_x_kernel<4, 3, false, true><<<gx, nssm::kConvXThreads, 0, st>>>(cp);
-    else nssm::conv_x_kernel<4, 3, false, false><<<gx, nssm::kConvXThreads, 0, st>>>(cp);
-  } else if (vec) {
-    if (iobf && wbf) nssm::conv_x_kernel<4, 4, true, true><<<gx, nssm::kConvXThreads, 0, st>>>(cp);
-    else if (iobf) nssm::conv_x_kernel<4, 4, true, false><<<gx, nssm::kConvXThreads, 0, st>>>(cp);
-    else if (wbf) nssm::conv_x_kernel<4, 4, false, true><<<gx, nssm::kConvXThreads, 0, st>>>(cp);
-    else nssm::conv_x_kernel<4, 4, false, false><<<gx, nssm::kConvXThreads, 0, st>>>(cp);
-  } else {
-    nssm::conv_x_kernel<0, 0, false, false><<<gx, nssm::kConvXThreads, 0, st>>>(cp);
+  if (!vec) return launch_conv<0, 0, false, false>(cp, a->batch, a->ngroups, st);
+  if (a->state_len == 3) {
+    if (iobf) return wbf ? launch_conv<4, 3, true, true>(cp, a->batch, a->ngroups, st)
+                         : launch_conv<4, 3, true, false>(cp, a->batch, a->ngroups, st);
+    return wbf ? launch_conv<4, 3, false, true>(cp, a->batch, a->ngroups, st)
+               : launch_conv<4, 3, false, false>(cp, a->batch, a->ngroups, st);
   }
-  int rc = cuda_check("conv_x_kernel launch");
-  if (rc) return rc;
-  dim3 grid((unsigned)((a->batch + nssm::kConvTile - 1) / nssm::kConvTile), (unsigned)a->ngroups, 2);
-  nssm::conv_step_kernel<128><<<grid, nssm::kConvThreads, smem, st>>>(cp);
-  return cuda_check("conv_step_kernel launch");
+  if (iobf) return wbf ? launch_conv<4, 4, true, true>(cp, a->batch, a->ngroups, st)
+                       : launch_conv<4, 4, true, false>(cp, a->batch, a->ngroups, st);
+  return wbf ? launch_conv<4, 4, false, true>(cp, a->batch, a->ngroups, st)
+             : launch_conv<4, 4, false, false>(cp, a->batch, a->ngroups, st);
 }
 
 size_t nssm_sizeof_conv_args(void) { return sizeof(nssm_conv_args); }

@@ -76,10 +76,118 @@ __device__ __forceinline__ float conv_channel(const ConvParams& p, int64_t srow,
   return p.act ? silu_f(acc) : acc;
 }
 
+// Four consecutive channels d0 .. d0+3 of one row with compile-time width K and state
+// length L: the loads (state, x) and the compute + stores are separate steps so a thread
+// can have several groups' loads in flight.  Every access is aligned (checked on the host).
+template <int L, bool IOBF>
+struct Conv4 {
+  float s[4 * L];
+  float x[4];
+};
+
+template <int L, bool IOBF>
+__device__ __forceinline__ void conv4_load(const ConvParams& p, int64_t srow, int b, int d0, Conv4<L, IOBF>& c) {
+  constexpr int EB = IOBF ? 2 : 4;
+  const unsigned char* sp = static_cast<const unsigned char*>(p.state) + (srow + (int64_t)d0 * L) * EB;
+  const int64_t xo = (int64_t)b * p.xbc_sb + d0;
+  if constexpr (IOBF) {
+#pragma unroll
+    for (int q = 0; q < L; ++q) {   // 4 * L bf16 = L x 8 bytes
+      const uint2 u = reinterpret_cast<const uint2*>(sp)[q];
+      c.s[4 * q + 0] = __uint_as_float(u.x << 16);
+      c.s[4 * q + 1] = __uint_as_float(u.x & 0xffff0000u);
+      c.s[4 * q + 2] = __uint_as_float(u.y << 16);
+      c.s[4 * q + 3] = __uint_as_float(u.y & 0xffff0000u);
+    }
+    const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(p.xbc) + xo);
+    c.x[0] = __uint_as_float(u.x << 16); c.x[1] = __uint_as_float(u.x & 0xffff0000u);
+    c.x[2] = __uint_as_float(u.y << 16); c.x[3] = __uint_as_float(u.y & 0xffff0000u);
+  } else {
+#pragma unroll
+    for (int q = 0; q < L; ++q) {
+      const float4 u = reinterpret_cast<const float4*>(sp)[q];
+      c.s[4 * q + 0] = u.x; c.s[4 * q + 1] = u.y; c.s[4 * q + 2] = u.z; c.s[4 * q + 3] = u.w;
+    }
+    const float4 u = *reinterpret_cast<const float4*>(static_cast<const float*>(p.xbc) + xo);
+    c.x[0] = u.x; c.x[1] = u.y; c.x[2] = u.z; c.x[3] = u.w;
+  }
+}
+
+// 4 * K weights and 4 biases of channels d0 .. d0+3 as fp32
+template <int K, bool WBF>
+__device__ __forceinline__ void conv4_weights(const ConvParams& p, int d0, float* w, float* bias) {
+  if constexpr (WBF) {
+    const uint4* wp = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.weight) + (int64_t)d0 * K);
+#pragma unroll
+    for (int q = 0; q < K / 2; ++q) {   // 8 bf16 per 16 bytes
+      const uint4 u = wp[q];
+      const uint32_t ww[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        w[8 * q + 2 * t] = __uint_as_float(ww[t] << 16);
+        w[8 * q + 2 * t + 1] = __uint_as_float(ww[t] & 0xffff0000u);
+      }
+    }
+    if (p.bias) {
+      const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(p.bias) + d0);
+      bias[0] = __uint_as_float(u.x << 16); bias[1] = __uint_as_float(u.x & 0xffff0000u);
+      bias[2] = __uint_as_float(u.y << 16); bias[3] = __uint_as_float(u.y & 0xffff0000u);
+    }
+  } else {
+    const float4* wp = reinterpret_cast<const float4*>(static_cast<const float*>(p.weight) + (int64_t)d0 * K);
+#pragma unroll
+    for (int q = 0; q < K; ++q) {
+      const float4 u = wp[q];
+      w[4 * q] = u.x; w[4 * q + 1] = u.y; w[4 * q + 2] = u.z; w[4 * q + 3] = u.w;
+    }
+    if (p.bias) {
+      const float4 u = *reinterpret_cast<const float4*>(static_cast<const float*>(p.bias) + d0);
+      bias[0] = u.x; bias[1] = u.y; bias[2] = u.z; bias[3] = u.w;
+    }
+  }
+}
+
+// conv outputs of the 4 channels (activated, fp32) and the state written back
+template <int K, int L, bool IOBF, bool WBF>
+__device__ __forceinline__ void conv4_finish(const ConvParams& p, int64_t srow, int d0, const Conv4<L, IOBF>& c,
+                                             float* out) {
+  float w[4 * K], bias[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  conv4_weights<K, WBF>(p, d0, w, bias);
+#pragma unroll
+  for (int ch = 0; ch < 4; ++ch) {
+    // window position l of [state, x] holds tap k = l - (L + 1 - K)
+    float acc = 0.0f;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const int l = L + 1 - K + k;
+      acc = fmaf(w[ch * K + k], l < L ? c.s[ch * L + l] : c.x[ch], acc);
+    }
+    if (p.bias) acc = acc + bias[ch];
+    out[ch] = p.act ? silu_f(acc) : acc;
+  }
+  // state <- last L of the window: element e = ch * L + l takes window position l + 1
+  constexpr int EB = IOBF ? 2 : 4;
+  unsigned char* sp = static_cast<unsigned char*>(p.state) + (srow + (int64_t)d0 * L) * EB;
+  auto nv = [&](int e) { const int ch = e / L, l = e % L; return l + 1 < L ? c.s[ch * L + l + 1] : c.x[ch]; };
+  if constexpr (IOBF) {
+#pragma unroll
+    for (int q = 0; q < L; ++q) {
+      uint32_t h[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) h[t] = __float_as_uint(nv(4 * q + t)) >> 16;   // bf16 values: exact
+      reinterpret_cast<uint2*>(sp)[q] = make_uint2(h[0] | (h[1] << 16), h[2] | (h[3] << 16));
+    }
+  } else {
+#pragma unroll
+    for (int q = 0; q < L; ++q)
+      reinterpret_cast<float4*>(sp)[q] = make_float4(nv(4 * q), nv(4 * q + 1), nv(4 * q + 2), nv(4 * q + 3));
+  }
+}
+
 // B and C channels.  grid (ceil(T / kConvTile), G, 2): z = 0 for B, 1 for C.  A CTA
 // converts the tile's channels of group g (state updated), then rotates them (all 128
 // outputs: thread tile of 4 rows x 8 outputs) or copies them out.
-template <int N>
+template <int N, int K, int L, bool IOBF, bool WBF>
 __global__ void __launch_bounds__(kConvThreads, 2) conv_step_kernel(const ConvParams p) {
   static_assert(N == 128, "tile mapping assumes dstate 128");
   extern __shared__ __align__(16) float csm_[];
@@ -109,19 +217,54 @@ __global__ void __launch_bounds__(kConvThreads, 2) conv_step_kernel(const ConvPa
     }
   }
 
-  // the tile's B (or C) channels of group g into shared memory (state updated)
+  // the tile's B (or C) channels of group g into shared memory (state updated), rounded
+  // to the io dtype
   {
     const int cbase = p.I + which * p.G * N + g * N;
-    for (int e = tid; e < kConvTile * N; e += kConvThreads) {
-      const int r = e / N, n = e - r * N;
-      float v = 0.0f;
-      if (r < nr) {
+    if constexpr (K > 0) {
+      // thread -> (row r, 4 channels) tasks, kTasks at a time with all loads first
+      constexpr int kQ = N / 4;
+      constexpr int kTasks = kConvTile * kQ / kConvThreads;   // 8
+      Conv4<L, IOBF> cin[kTasks];
+      int64_t srow[kTasks];
+#pragma unroll
+      for (int u = 0; u < kTasks; ++u) {
+        const int e = tid + u * kConvThreads;
+        const int r = e / kQ, d0 = cbase + 4 * (e % kQ);
         const int b = b0 + r;
-        const int slot = p.idx ? p.idx[b] : b;
-        if (slot != p.pad && slot >= 0 && slot < p.S)
-          v = round_io(conv_channel(p, (int64_t)slot * p.state_ss, b, cbase + n, true), p.dtype);
+        srow[u] = -1;
+        if (r < nr) {
+          const int slot = p.idx ? p.idx[b] : b;
+          if (slot != p.pad && slot >= 0 && slot < p.S) {
+            srow[u] = (int64_t)slot * p.state_ss;
+            conv4_load<L, IOBF>(p, srow[u], b, d0, cin[u]);
+          }
+        }
       }
-      Xs[r * kRotLd + n] = v;
+#pragma unroll
+      for (int u = 0; u < kTasks; ++u) {
+        const int e = tid + u * kConvThreads;
+        const int r = e / kQ, n0 = 4 * (e % kQ);
+        float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        if (srow[u] >= 0) {
+          conv4_finish<K, L, IOBF, WBF>(p, srow[u], cbase + n0, cin[u], o);
+#pragma unroll
+          for (int t = 0; t < 4; ++t) o[t] = round_io(o[t], p.dtype);
+        }
+        *reinterpret_cast<float4*>(Xs + r * kRotLd + n0) = make_float4(o[0], o[1], o[2], o[3]);
+      }
+    } else {
+      for (int e = tid; e < kConvTile * N; e += kConvThreads) {
+        const int r = e / N, n = e - r * N;
+        float v = 0.0f;
+        if (r < nr) {
+          const int b = b0 + r;
+          const int slot = p.idx ? p.idx[b] : b;
+          if (slot != p.pad && slot >= 0 && slot < p.S)
+            v = round_io(conv_channel(p, (int64_t)slot * p.state_ss, b, cbase + n, true), p.dtype);
+        }
+        Xs[r * kRotLd + n] = v;
+      }
     }
   }
   __syncthreads();
@@ -170,8 +313,8 @@ __global__ void __launch_bounds__(kConvThreads, 2) conv_step_kernel(const ConvPa
 }
 
 // x channels: one thread per 4 consecutive channels of one row.  With compile-time K and L
-// (VEC) the state, weights and x move in 8-byte vectors (16 for fp32 weights); otherwise
-// per element.  grid (ceil(I / (4 * kConvXThreads)), T).
+// the state, weights and x move in 8- or 16-byte vectors; otherwise per element.
+// grid (ceil(I / (4 * kConvXThreads)), T).
 constexpr int kConvXThreads = 256;
 
 template <int K, int L, bool IOBF, bool WBF>
@@ -187,90 +330,16 @@ __global__ void __launch_bounds__(kConvXThreads) conv_x_kernel(const ConvParams 
   }
   const int64_t srow = (int64_t)slot * p.state_ss;
   if constexpr (K > 0) {
-    // every access below is aligned (checked on the host): state rows of L elements start
-    // at d0 * L, x rows at b * xbc_sb + d0
-    constexpr int EB = IOBF ? 2 : 4;
-    float win[4][L + 1];
-    {
-      // 4 * L state elements, contiguous
-      const unsigned char* sp = static_cast<const unsigned char*>(p.state) + (srow + (int64_t)d0 * L) * EB;
-      float sv[4 * L];
-      if constexpr (IOBF) {
-#pragma unroll
-        for (int q = 0; q < L; ++q) {   // 4 * L bf16 = L x 8 bytes
-          const uint2 u = reinterpret_cast<const uint2*>(sp)[q];
-          sv[4 * q + 0] = __uint_as_float(u.x << 16);
-          sv[4 * q + 1] = __uint_as_float(u.x & 0xffff0000u);
-          sv[4 * q + 2] = __uint_as_float(u.y << 16);
-          sv[4 * q + 3] = __uint_as_float(u.y & 0xffff0000u);
-        }
-      } else {
-#pragma unroll
-        for (int q = 0; q < L; ++q) {
-          const float4 u = reinterpret_cast<const float4*>(sp)[q];
-          sv[4 * q + 0] = u.x; sv[4 * q + 1] = u.y; sv[4 * q + 2] = u.z; sv[4 * q + 3] = u.w;
-        }
-      }
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-#pragma unroll
-        for (int l = 0; l < L; ++l) win[c][l] = sv[c * L + l];
-    }
-    {
-      const int64_t xo = (int64_t)b * p.xbc_sb + d0;
-      float xv[4];
-      if constexpr (IOBF) {
-        const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(p.xbc) + xo);
-        xv[0] = __uint_as_float(u.x << 16); xv[1] = __uint_as_float(u.x & 0xffff0000u);
-        xv[2] = __uint_as_float(u.y << 16); xv[3] = __uint_as_float(u.y & 0xffff0000u);
-      } else {
-        const float4 u = *reinterpret_cast<const float4*>(static_cast<const float*>(p.xbc) + xo);
-        xv[0] = u.x; xv[1] = u.y; xv[2] = u.z; xv[3] = u.w;
-      }
-#pragma unroll
-      for (int c = 0; c < 4; ++c) win[c][L] = xv[c];
-    }
-    float wv[4 * K];
-#pragma unroll
-    for (int e = 0; e < 4 * K; ++e) wv[e] = ld_io(p.weight, (int64_t)d0 * K + e, WBF ? NSSM_BF16 : NSSM_F32);
+    Conv4<L, IOBF> cin;
+    conv4_load<L, IOBF>(p, srow, b, d0, cin);
     float out[4];
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      float acc = 0.0f;
-#pragma unroll
-      for (int k = 0; k < K; ++k) acc = fmaf(wv[c * K + k], win[c][L + 1 - K + k], acc);
-      if (p.bias) acc = acc + ld_io(p.bias, d0 + c, WBF ? NSSM_BF16 : NSSM_F32);
-      out[c] = p.act ? silu_f(acc) : acc;
-    }
-    // state <- last L of the window
-    unsigned char* sp = static_cast<unsigned char*>(p.state) + (srow + (int64_t)d0 * L) * EB;
+    conv4_finish<K, L, IOBF, WBF>(p, srow, d0, cin, out);
     if constexpr (IOBF) {
-#pragma unroll
-      for (int q = 0; q < L; ++q) {
-        const int e0 = 4 * q;
-        uint32_t h[4];
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const int e = e0 + t, c = e / L, l = e % L;
-          h[t] = __float_as_uint(win[c][l + 1]) >> 16;   // bf16 values: exact
-        }
-        reinterpret_cast<uint2*>(sp)[q] = make_uint2(h[0] | (h[1] << 16), h[2] | (h[3] << 16));
-      }
       const __nv_bfloat162 o01 = __floats2bfloat162_rn(out[0], out[1]);
       const __nv_bfloat162 o23 = __floats2bfloat162_rn(out[2], out[3]);
       *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p.x_out) + (int64_t)b * p.x_sb + d0) =
           make_uint2(*reinterpret_cast<const uint32_t*>(&o01), *reinterpret_cast<const uint32_t*>(&o23));
     } else {
-#pragma unroll
-      for (int q = 0; q < L; ++q) {
-        float v4[4];
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const int e = 4 * q + t, c = e / L, l = e % L;
-          v4[t] = win[c][l + 1];
-        }
-        reinterpret_cast<float4*>(sp)[q] = make_float4(v4[0], v4[1], v4[2], v4[3]);
-      }
       *reinterpret_cast<float4*>(static_cast<float*>(p.x_out) + (int64_t)b * p.x_sb + d0) =
           make_float4(out[0], out[1], out[2], out[3]);
     }

@@ -156,8 +156,10 @@ typedef struct {
   int32_t pad_slot_id;
   const void* xbc;        /* [batch][conv_dim]                                    */
   int64_t xbc_stride_b;
-  void* conv_state;       /* [num_slots][conv_dim][state_len]                     */
-  int64_t state_stride_s;
+  void* conv_state;       /* element (s, d, l) at s*stride_s + d*stride_d + l*stride_l: */
+  int64_t state_stride_s; /* [num_slots][conv_dim][state_len] (stride_d = L, stride_l = 1) */
+  int64_t state_stride_d; /* or the HF / vLLM cache layout (stride_d = 1,               */
+  int64_t state_stride_l; /*   stride_l = conv_dim)                                    */
   const void* weight;     /* [conv_dim][width]                                    */
   const void* bias;       /* [conv_dim] or NULL                                   */
   const float* R;         /* [ngroups][dstate][dstate] or NULL (no rotation)      */

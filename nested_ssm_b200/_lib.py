@@ -64,7 +64,8 @@ class NssmConvArgs(C.Structure):
         ("io_dtype", C.c_int32), ("weight_dtype", C.c_int32), ("activation", C.c_int32),
         ("pad_slot_id", C.c_int32),
         ("xbc", C.c_void_p), ("xbc_stride_b", C.c_int64),
-        ("conv_state", C.c_void_p), ("state_stride_s", C.c_int64),
+        ("conv_state", C.c_void_p), ("state_stride_s", C.c_int64), ("state_stride_d", C.c_int64),
+        ("state_stride_l", C.c_int64),
         ("weight", C.c_void_p), ("bias", C.c_void_p), ("R", C.c_void_p),
         ("state_batch_indices", C.c_void_p),
         ("x_out", C.c_void_p), ("x_out_stride_b", C.c_int64),

@@ -172,7 +172,7 @@ int maybe_rotate(const nssm_step_args* a, int G, int N, nssm::StepParams& sp, cu
   return NSSM_OK;
 }
 
-template <int K, int L, bool IOBF, bool WBF>
+template <int K, int L, bool IOBF, bool WBF, bool LD>
 int launch_conv(const nssm::ConvParams& cp, int batch, int G, cudaStream_t st) {
   // the B/C kernel uses 84 KB of dynamic shared memory: opt in once per device
   static std::atomic<unsigned long long> attr_done{0};
@@ -180,14 +180,14 @@ int launch_conv(const nssm::ConvParams& cp, int batch, int G, cudaStream_t st) {
   if (cudaGetDevice(&dev) != cudaSuccess) return cuda_check("cudaGetDevice");
   const unsigned long long bit = 1ull << (dev & 63);
   constexpr int smem = nssm::conv_smem_bytes(128);
-  auto kbc = nssm::conv_step_kernel<128, K, L, IOBF, WBF>;
+  auto kbc = nssm::conv_step_kernel<128, K, L, IOBF, WBF, LD>;
   if (!(attr_done.load(std::memory_order_acquire) & bit)) {
     if (cudaFuncSetAttribute(kbc, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
       return cuda_check("cudaFuncSetAttribute(conv_step_kernel)");
     attr_done.fetch_or(bit, std::memory_order_acq_rel);
   }
   dim3 gx((unsigned)((cp.I + 4 * nssm::kConvXThreads - 1) / (4 * nssm::kConvXThreads)), (unsigned)batch);
-  nssm::conv_x_kernel<K, L, IOBF, WBF><<<gx, nssm::kConvXThreads, 0, st>>>(cp);
+  nssm::conv_x_kernel<K, L, IOBF, WBF, LD><<<gx, nssm::kConvXThreads, 0, st>>>(cp);
   int rc = cuda_check("conv_x_kernel launch");
   if (rc) return rc;
   dim3 grid((unsigned)((batch + nssm::kConvTile - 1) / nssm::kConvTile), (unsigned)G, 2);
@@ -333,6 +333,7 @@ int nssm_conv_step(const nssm_conv_args* a, void* stream) {
   nssm::ConvParams cp{};
   cp.xbc = a->xbc; cp.xbc_sb = a->xbc_stride_b;
   cp.state = a->conv_state; cp.state_ss = a->state_stride_s; cp.L = a->state_len; cp.K = a->width;
+  cp.state_sd = a->state_stride_d; cp.state_sl = a->state_stride_l;
   cp.weight = a->weight; cp.w_dtype = a->weight_dtype; cp.bias = a->bias; cp.act = a->activation;
   cp.R = a->R; cp.idx = a->state_batch_indices; cp.pad = a->pad_slot_id; cp.S = a->num_slots;
   cp.T = a->batch; cp.I = a->nheads * a->headdim; cp.G = a->ngroups; cp.dtype = a->io_dtype;
@@ -340,24 +341,31 @@ int nssm_conv_step(const nssm_conv_args* a, void* stream) {
   cp.b_out = a->B_out; cp.c_out = a->C_out; cp.bc_sb = a->bc_out_stride_b;
   cp.status = a->status;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // vector paths for width 4 with state length 3 or 4 when every access is aligned
-  const int eb = a->io_dtype == NSSM_BF16 ? 2 : 4;
-  const bool vec = a->width == 4 && (a->state_len == 3 || a->state_len == 4) && cp.I % 4 == 0 &&
+  // vector paths for width 4 with state length 3 or 4 when every access is aligned; the
+  // state either [slot][d][l] (DL) or channels-last [slot][l][d] (LD)
+  const bool dl = a->state_stride_l == 1 && a->state_stride_d == a->state_len;
+  const bool ld = a->state_stride_d == 1 && a->state_stride_l % 4 == 0 && a->state_stride_l >= cp.I + 2 * a->ngroups * 128;
+  const bool vec = a->width == 4 && (a->state_len == 3 || a->state_len == 4) && cp.I % 4 == 0 && (dl || ld) &&
                    aligned16(a->xbc) && aligned16(a->conv_state) && aligned16(a->x_out) && aligned16(a->weight) &&
                    (!a->bias || aligned16(a->bias)) && a->xbc_stride_b % 4 == 0 && a->x_out_stride_b % 4 == 0 &&
-                   a->state_stride_s % 4 == 0 && ((int64_t)a->state_len * 4 * eb) % (eb == 2 ? 8 : 16) == 0;
+                   a->state_stride_s % 4 == 0;
   const bool iobf = a->io_dtype == NSSM_BF16, wbf = a->weight_dtype == NSSM_BF16;
-  if (!vec) return launch_conv<0, 0, false, false>(cp, a->batch, a->ngroups, st);
-  if (a->state_len == 3) {
-    if (iobf) return wbf ? launch_conv<4, 3, true, true>(cp, a->batch, a->ngroups, st)
-                         : launch_conv<4, 3, true, false>(cp, a->batch, a->ngroups, st);
-    return wbf ? launch_conv<4, 3, false, true>(cp, a->batch, a->ngroups, st)
-               : launch_conv<4, 3, false, false>(cp, a->batch, a->ngroups, st);
+  const int B = a->batch, G = a->ngroups;
+  if (!vec) return launch_conv<0, 0, false, false, false>(cp, B, G, st);
+  if (ld) {
+    if (a->state_len == 3) {
+      if (iobf) return wbf ? launch_conv<4, 3, true, true, true>(cp, B, G, st) : launch_conv<4, 3, true, false, true>(cp, B, G, st);
+      return wbf ? launch_conv<4, 3, false, true, true>(cp, B, G, st) : launch_conv<4, 3, false, false, true>(cp, B, G, st);
+    }
+    if (iobf) return wbf ? launch_conv<4, 4, true, true, true>(cp, B, G, st) : launch_conv<4, 4, true, false, true>(cp, B, G, st);
+    return wbf ? launch_conv<4, 4, false, true, true>(cp, B, G, st) : launch_conv<4, 4, false, false, true>(cp, B, G, st);
   }
-  if (iobf) return wbf ? launch_conv<4, 4, true, true>(cp, a->batch, a->ngroups, st)
-                       : launch_conv<4, 4, true, false>(cp, a->batch, a->ngroups, st);
-  return wbf ? launch_conv<4, 4, false, true>(cp, a->batch, a->ngroups, st)
-             : launch_conv<4, 4, false, false>(cp, a->batch, a->ngroups, st);
+  if (a->state_len == 3) {
+    if (iobf) return wbf ? launch_conv<4, 3, true, true, false>(cp, B, G, st) : launch_conv<4, 3, true, false, false>(cp, B, G, st);
+    return wbf ? launch_conv<4, 3, false, true, false>(cp, B, G, st) : launch_conv<4, 3, false, false, false>(cp, B, G, st);
+  }
+  if (iobf) return wbf ? launch_conv<4, 4, true, true, false>(cp, B, G, st) : launch_conv<4, 4, true, false, false>(cp, B, G, st);
+  return wbf ? launch_conv<4, 4, false, true, false>(cp, B, G, st) : launch_conv<4, 4, false, false, false>(cp, B, G, st);
 }
 
 size_t nssm_sizeof_conv_args(void) { return sizeof(nssm_conv_args); }

@@ -18,7 +18,8 @@ struct ConvParams {
   const void* xbc;
   int64_t xbc_sb;
   void* state;
-  int64_t state_ss;     // elements between slots
+  int64_t state_ss;     // element (s, d, l) at s * state_ss + d * state_sd + l * state_sl
+  int64_t state_sd, state_sl;
   int L, K;
   const void* weight;
   int w_dtype;
@@ -55,11 +56,11 @@ __device__ __forceinline__ float round_io(float v, int dtype) {
 // k = l - (L + 1 - K)); updates the slot's state when `upd`
 __device__ __forceinline__ float conv_channel(const ConvParams& p, int64_t srow, int b, int d, bool upd) {
   const float xin = ld_io(p.xbc, (int64_t)b * p.xbc_sb + d, p.dtype);
-  const int64_t so = srow + (int64_t)d * p.L;
+  const int64_t so = srow + (int64_t)d * p.state_sd;
   float win[kConvMaxL + 1];
 #pragma unroll
   for (int l = 0; l <= kConvMaxL; ++l)
-    win[l] = l < p.L ? ld_io(p.state, so + l, p.dtype) : (l == p.L ? xin : 0.0f);
+    win[l] = l < p.L ? ld_io(p.state, so + l * p.state_sl, p.dtype) : (l == p.L ? xin : 0.0f);
   float acc = 0.0f;
   const int off = p.L + 1 - p.K;
 #pragma unroll
@@ -71,7 +72,7 @@ __device__ __forceinline__ float conv_channel(const ConvParams& p, int64_t srow,
   if (upd) {
 #pragma unroll
     for (int l = 0; l < kConvMaxL; ++l)
-      if (l < p.L) st_io(p.state, so + l, p.dtype, win[l + 1]);
+      if (l < p.L) st_io(p.state, so + l * p.state_sl, p.dtype, win[l + 1]);
   }
   return p.act ? silu_f(acc) : acc;
 }
@@ -85,14 +86,34 @@ struct Conv4 {
   float x[4];
 };
 
-template <int L, bool IOBF>
+// LD: the state is channels-last ([slot][l][d], the HF / vLLM cache layout): each window
+// position of the 4 channels is one vector; otherwise [slot][d][l]: the 4 channels' L
+// positions are 4 * L consecutive elements.  c.s[ch * L + l] either way.
+template <int L, bool IOBF, bool LD>
 __device__ __forceinline__ void conv4_load(const ConvParams& p, int64_t srow, int b, int d0, Conv4<L, IOBF>& c) {
   constexpr int EB = IOBF ? 2 : 4;
-  const unsigned char* sp = static_cast<const unsigned char*>(p.state) + (srow + (int64_t)d0 * L) * EB;
   const int64_t xo = (int64_t)b * p.xbc_sb + d0;
+  if constexpr (LD) {
+#pragma unroll
+    for (int l = 0; l < L; ++l) {
+      const int64_t e = srow + (int64_t)l * p.state_sl + d0;
+      float v[4];
+      if constexpr (IOBF) {
+        const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(p.state) + e);
+        v[0] = __uint_as_float(u.x << 16); v[1] = __uint_as_float(u.x & 0xffff0000u);
+        v[2] = __uint_as_float(u.y << 16); v[3] = __uint_as_float(u.y & 0xffff0000u);
+      } else {
+        const float4 u = *reinterpret_cast<const float4*>(static_cast<const float*>(p.state) + e);
+        v[0] = u.x; v[1] = u.y; v[2] = u.z; v[3] = u.w;
+      }
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch) c.s[ch * L + l] = v[ch];
+    }
+  }
+  const unsigned char* sp = static_cast<const unsigned char*>(p.state) + (srow + (int64_t)d0 * L) * EB;
   if constexpr (IOBF) {
 #pragma unroll
-    for (int q = 0; q < L; ++q) {   // 4 * L bf16 = L x 8 bytes
+    for (int q = 0; q < (LD ? 0 : L); ++q) {   // 4 * L bf16 = L x 8 bytes
       const uint2 u = reinterpret_cast<const uint2*>(sp)[q];
       c.s[4 * q + 0] = __uint_as_float(u.x << 16);
       c.s[4 * q + 1] = __uint_as_float(u.x & 0xffff0000u);
@@ -104,7 +125,7 @@ __device__ __forceinline__ void conv4_load(const ConvParams& p, int64_t srow, in
     c.x[2] = __uint_as_float(u.y << 16); c.x[3] = __uint_as_float(u.y & 0xffff0000u);
   } else {
 #pragma unroll
-    for (int q = 0; q < L; ++q) {
+    for (int q = 0; q < (LD ? 0 : L); ++q) {
       const float4 u = reinterpret_cast<const float4*>(sp)[q];
       c.s[4 * q + 0] = u.x; c.s[4 * q + 1] = u.y; c.s[4 * q + 2] = u.z; c.s[4 * q + 3] = u.w;
     }
@@ -148,7 +169,7 @@ __device__ __forceinline__ void conv4_weights(const ConvParams& p, int d0, float
 }
 
 // conv outputs of the 4 channels (activated, fp32) and the state written back
-template <int K, int L, bool IOBF, bool WBF>
+template <int K, int L, bool IOBF, bool WBF, bool LD>
 __device__ __forceinline__ void conv4_finish(const ConvParams& p, int64_t srow, int d0, const Conv4<L, IOBF>& c,
                                              float* out) {
   float w[4 * K], bias[4] = {0.0f, 0.0f, 0.0f, 0.0f};
@@ -167,8 +188,25 @@ __device__ __forceinline__ void conv4_finish(const ConvParams& p, int64_t srow, 
   }
   // state <- last L of the window: element e = ch * L + l takes window position l + 1
   constexpr int EB = IOBF ? 2 : 4;
-  unsigned char* sp = static_cast<unsigned char*>(p.state) + (srow + (int64_t)d0 * L) * EB;
   auto nv = [&](int e) { const int ch = e / L, l = e % L; return l + 1 < L ? c.s[ch * L + l + 1] : c.x[ch]; };
+  if constexpr (LD) {
+#pragma unroll
+    for (int l = 0; l < L; ++l) {
+      const int64_t e = srow + (int64_t)l * p.state_sl + d0;
+      if constexpr (IOBF) {
+        uint32_t h[4];
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) h[ch] = __float_as_uint(nv(ch * L + l)) >> 16;   // bf16 values: exact
+        *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p.state) + e) =
+            make_uint2(h[0] | (h[1] << 16), h[2] | (h[3] << 16));
+      } else {
+        *reinterpret_cast<float4*>(static_cast<float*>(p.state) + e) =
+            make_float4(nv(l), nv(L + l), nv(2 * L + l), nv(3 * L + l));
+      }
+    }
+    return;
+  }
+  unsigned char* sp = static_cast<unsigned char*>(p.state) + (srow + (int64_t)d0 * L) * EB;
   if constexpr (IOBF) {
 #pragma unroll
     for (int q = 0; q < L; ++q) {
@@ -187,7 +225,7 @@ __device__ __forceinline__ void conv4_finish(const ConvParams& p, int64_t srow, 
 // B and C channels.  grid (ceil(T / kConvTile), G, 2): z = 0 for B, 1 for C.  A CTA
 // converts the tile's channels of group g (state updated), then rotates them (all 128
 // outputs: thread tile of 4 rows x 8 outputs) or copies them out.
-template <int N, int K, int L, bool IOBF, bool WBF>
+template <int N, int K, int L, bool IOBF, bool WBF, bool LD>
 __global__ void __launch_bounds__(kConvThreads, 2) conv_step_kernel(const ConvParams p) {
   static_assert(N == 128, "tile mapping assumes dstate 128");
   extern __shared__ __align__(16) float csm_[];
@@ -237,7 +275,7 @@ __global__ void __launch_bounds__(kConvThreads, 2) conv_step_kernel(const ConvPa
           const int slot = p.idx ? p.idx[b] : b;
           if (slot != p.pad && slot >= 0 && slot < p.S) {
             srow[u] = (int64_t)slot * p.state_ss;
-            conv4_load<L, IOBF>(p, srow[u], b, d0, cin[u]);
+            conv4_load<L, IOBF, LD>(p, srow[u], b, d0, cin[u]);
           }
         }
       }
@@ -247,7 +285,7 @@ __global__ void __launch_bounds__(kConvThreads, 2) conv_step_kernel(const ConvPa
         const int r = e / kQ, n0 = 4 * (e % kQ);
         float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
         if (srow[u] >= 0) {
-          conv4_finish<K, L, IOBF, WBF>(p, srow[u], cbase + n0, cin[u], o);
+          conv4_finish<K, L, IOBF, WBF, LD>(p, srow[u], cbase + n0, cin[u], o);
 #pragma unroll
           for (int t = 0; t < 4; ++t) o[t] = round_io(o[t], p.dtype);
         }
@@ -317,7 +355,7 @@ __global__ void __launch_bounds__(kConvThreads, 2) conv_step_kernel(const ConvPa
 // grid (ceil(I / (4 * kConvXThreads)), T).
 constexpr int kConvXThreads = 256;
 
-template <int K, int L, bool IOBF, bool WBF>
+template <int K, int L, bool IOBF, bool WBF, bool LD>
 __global__ void __launch_bounds__(kConvXThreads) conv_x_kernel(const ConvParams p) {
   const int b = blockIdx.y;
   const int d0 = (blockIdx.x * kConvXThreads + threadIdx.x) * 4;
@@ -331,9 +369,9 @@ __global__ void __launch_bounds__(kConvXThreads) conv_x_kernel(const ConvParams 
   const int64_t srow = (int64_t)slot * p.state_ss;
   if constexpr (K > 0) {
     Conv4<L, IOBF> cin;
-    conv4_load<L, IOBF>(p, srow, b, d0, cin);
+    conv4_load<L, IOBF, LD>(p, srow, b, d0, cin);
     float out[4];
-    conv4_finish<K, L, IOBF, WBF>(p, srow, d0, cin, out);
+    conv4_finish<K, L, IOBF, WBF, LD>(p, srow, d0, cin, out);
     if constexpr (IOBF) {
       const __nv_bfloat162 o01 = __floats2bfloat162_rn(out[0], out[1]);
       const __nv_bfloat162 o23 = __floats2bfloat162_rn(out[2], out[3]);

@@ -259,8 +259,9 @@ def conv_step(xbc: torch.Tensor, conv_state: torch.Tensor, weight: torch.Tensor,
               x_out=None, B_out=None, C_out=None, status=None):
     """Decode-token conv of one layer ahead of the state update: the causal conv1d update
     of ``xbc [b, conv_dim]`` (the in_proj slice [x | B | C]) with ``conv_state
-    [num_slots, conv_dim, L]`` (updated in place, rows by ``conv_state_indices``), the
-    activation, the split, and the rotation of B and C by ``R [G, N, N]``.
+    [num_slots, conv_dim, L]`` (updated in place, rows by ``conv_state_indices``; L
+    innermost, or channels-last as the HF cache keeps it), the activation, the split, and
+    the rotation of B and C by ``R [G, N, N]``.
 
     Replaces ``causal_conv1d_update`` + split + the R einsums of
     scale/v4_fused_decode.py:39-48.  Returns ``(x [b, H, P], B [b, G, N], C [b, G, N])`` in
@@ -276,8 +277,10 @@ def conv_step(xbc: torch.Tensor, conv_state: torch.Tensor, weight: torch.Tensor,
     if conv_state.dim() != 3 or conv_state.shape[1] != conv_dim or conv_state.dtype != xbc.dtype:
         raise ValueError(f"conv_state must be [S, {conv_dim}, L] of xbc's dtype, got {tuple(conv_state.shape)} "
                          f"{conv_state.dtype}")
-    if conv_state.stride(2) != 1 or conv_state.stride(1) != conv_state.shape[2]:
-        raise ValueError("conv_state rows must be contiguous ([S, conv_dim, L] with L innermost)")
+    L = conv_state.shape[2]
+    if not ((conv_state.stride(2) == 1 and conv_state.stride(1) == L)          # [S, conv_dim, L]
+            or (conv_state.stride(1) == 1 and conv_state.stride(2) >= conv_dim)):   # channels-last (HF cache)
+        raise ValueError("conv_state must be laid out [S, conv_dim, L] (L innermost) or channels-last")
     w = weight.reshape(weight.shape[0], -1) if weight.dim() == 3 else weight     # HF conv1d [D, 1, K]
     if w.dim() != 2 or w.shape[0] != conv_dim or not w.is_contiguous() or w.dtype not in (torch.bfloat16, torch.float32):
         raise ValueError(f"weight must be a contiguous [{conv_dim}, K] (or [{conv_dim}, 1, K]) bf16 / fp32 tensor")
@@ -313,6 +316,7 @@ def conv_step(xbc: torch.Tensor, conv_state: torch.Tensor, weight: torch.Tensor,
     a.pad_slot_id = int(pad_slot_id)
     a.xbc, a.xbc_stride_b = xbc.data_ptr(), xbc.stride(0)
     a.conv_state, a.state_stride_s = conv_state.data_ptr(), conv_state.stride(0)
+    a.state_stride_d, a.state_stride_l = conv_state.stride(1), conv_state.stride(2)
     a.weight, a.bias, a.R = w.data_ptr(), _ptr(bias), _ptr(Rf)
     a.state_batch_indices = _ptr(idx)
     a.x_out, a.x_out_stride_b = x_out.data_ptr(), I

@@ -23,6 +23,11 @@ regenerate (checksums stored beside the outputs):
   a conv state advanced by the transformers cache roll) and the reference's own
   ``ActRotMask`` (``scale/nemotron_retrofit.py:18-54``: SiLU, then the rotation of B and C)
   as the activation, so y covers conv + SiLU + split + rotation + tiered state op.
+* ``hf_generate.npz`` -- the reference's HF integration end to end: a small random NemotronH
+  (two Mamba2 layers and one attention layer, seeded), its mixers' activation wrapped in the
+  reference's ``ActRotMask`` with seeded rotations, ``install(model, pb=32, c=4,
+  cold_bf16=0)`` (``scale/v4_native_decode.py:247-256``, the HF torch prefill), then greedy
+  ``generate``: the tokens and the logits of every step.
 """
 from __future__ import annotations
 
@@ -46,6 +51,27 @@ NATIVE = dict(b=2, H=16, P=80, N=128, G=2, pb=32, c=4, seed=11, steps=13, steps_
 VLLM = dict(b=2, S=4, H=8, P=80, N=128, G=2, pb=32, c=4, seed=12, steps=9, slots=[2, 0])
 ROT = dict(T=6, G=2, N=128, seed=13)
 CONV = dict(b=2, H=16, P=80, N=128, G=2, pb=32, c=4, seed=14, steps=9, K=4)
+HF = dict(b=2, prompt=7, new=9, seed=15, pb=32, c=4)
+
+
+def hf_model(seed: int):
+    """The small NemotronH of hf_generate.npz (fp32, CPU), built from its seed."""
+    from transformers import NemotronHConfig, NemotronHForCausalLM
+    cfg = NemotronHConfig(hidden_size=64, num_hidden_layers=3, mamba_num_heads=8, mamba_head_dim=32,
+                          ssm_state_size=128, n_groups=2, vocab_size=100, hybrid_override_pattern="M*M",
+                          num_attention_heads=4, num_key_value_heads=2, head_dim=16)
+    torch.manual_seed(seed)
+    return NemotronHForCausalLM(cfg).float().eval()
+
+
+def hf_rotations(model, seed: int):
+    """Seeded per-group orthogonal rotations, one per Mamba2 mixer."""
+    g = torch.Generator().manual_seed(seed + 1)
+    out = []
+    for m in model.modules():
+        if type(m).__name__ == "NemotronHMamba2Mixer":
+            out.append(torch.linalg.qr(torch.randn(m.n_groups, m.ssm_state_size, m.ssm_state_size, generator=g))[0])
+    return out
 
 
 def state0(b, H, P, N, seed):
@@ -257,6 +283,28 @@ def make_native_conv(ref):
     return arrays
 
 
+def make_hf(ref):
+    sys.path.insert(0, os.path.join(ref, "scale"))
+    import v4_native_decode as V
+    import nemotron_retrofit as NR
+    cfg = HF
+    model = hf_model(cfg["seed"])
+    Rs = hf_rotations(model, cfg["seed"])
+    mixers = [m for m in model.modules() if type(m).__name__ == "NemotronHMamba2Mixer"]
+    for m, R in zip(mixers, Rs):
+        act = NR.ActRotMask(m.act, m.intermediate_size, m.n_groups, m.ssm_state_size)
+        act.R.data.copy_(R)
+        m.act = act
+    V.install(model, pb=cfg["pb"], c=cfg["c"], cold_bf16=0)
+    for m in mixers:
+        m.v4cfg["lean_prefill"] = 0          # the HF torch prefill (no fused kernels on CPU)
+    g = torch.Generator().manual_seed(cfg["seed"] + 2)
+    ids = torch.randint(0, 100, (cfg["b"], cfg["prompt"]), generator=g)
+    out = model.generate(ids, max_new_tokens=cfg["new"], do_sample=False, output_logits=True,
+                         return_dict_in_generate=True)
+    return dict(ids=ids, tokens=out.sequences, logits=torch.stack(out.logits).float())
+
+
 def save(name, arrays):
     np_arrays = {k: (v.view(torch.int16) if v.dtype == torch.bfloat16 else v).numpy() for k, v in arrays.items()}
     path = os.path.join(HERE, name)
@@ -274,6 +322,7 @@ def main():
         save("vllm_fp8.npz", make_vllm(a.reference))
         save("rot_flat.npz", make_rot(a.reference))
         save("native_decode_conv.npz", make_native_conv(a.reference))
+        save("hf_generate.npz", make_hf(a.reference))
 
 
 if __name__ == "__main__":

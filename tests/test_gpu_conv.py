@@ -32,11 +32,12 @@ def _close_io(got, want, what):
     assert float((err > 0).float().mean()) <= 2e-2, f"{what}: differs too often"
 
 
-@pytest.mark.parametrize("K,L,wdt,rot", [(4, 3, torch.bfloat16, True), (4, 4, torch.float32, True),
-                                         (4, 3, torch.float32, False), (3, 2, torch.bfloat16, True)])
-def test_conv_step_matches_oracle(K, L, wdt, rot):
-    """Width 4 with state length 3 or 4 runs the vectorised x-channel kernel, other shapes
-    the per-element one."""
+@pytest.mark.parametrize("K,L,wdt,rot,last", [(4, 3, torch.bfloat16, True, False), (4, 4, torch.float32, True, False),
+                                              (4, 3, torch.float32, False, False), (3, 2, torch.bfloat16, True, False),
+                                              (4, 4, torch.bfloat16, True, True), (3, 3, torch.float32, False, True)])
+def test_conv_step_matches_oracle(K, L, wdt, rot, last):
+    """Width 4 with state length 3 or 4 runs the vectorised kernels, other shapes the
+    per-element ones; ``last``: the conv state channels-last, as the HF cache keeps it."""
     from nested_ssm_b200 import conv_step
     gen = torch.Generator().manual_seed(7 + L)
     S, b = 12, 9
@@ -46,7 +47,11 @@ def test_conv_step_matches_oracle(K, L, wdt, rot):
     bias = (torch.randn(D, generator=gen) * 0.1).to(wdt)
     R = O.make_params(H, G, N, seed=3)[0]["R"] if rot else None
     ostate = state0.clone()
-    gstate = state0.cuda()
+    if last:
+        gstate = torch.empty(S, L, D, dtype=torch.bfloat16, device="cuda").transpose(1, 2)
+        gstate.copy_(state0)
+    else:
+        gstate = state0.cuda()
     for step in range(3):
         xbc = torch.randn(b, D, generator=gen).to(torch.bfloat16)
         out = O.conv_step(ostate, slots, xbc, weight, bias, "silu")

@@ -37,6 +37,8 @@
  *        rotation of scale/v4_fused_decode.py:45-48.
  *  - nssm_materialize  : no single reference function; returns the exact full
  *        state the native path keeps in cache (scale/v4_native_decode.py:65-67).
+ *  - nssm_gated_rmsnorm: the mixer's norm(y, gate) after the state op
+ *        (scale/v4_native_decode.py:171; scale/nemotron_retrofit.py:146-161).
  *  - nssm_conv_step    : causal_conv1d_update + split + the post-conv R rotation of
  *        _v4_fused_decode (scale/v4_fused_decode.py:39-48); the HF decode branch's
  *        conv-state roll + weighted sum + act (scale/v4_native_decode.py:36-49).
@@ -174,6 +176,17 @@ typedef struct {
 
 NSSM_API int nssm_conv_step(const nssm_conv_args* args, void* stream);
 NSSM_API size_t nssm_sizeof_conv_args(void);
+
+/* Gated RMS norm of the mixer output (the step after the state op), one launch:
+ * h = y * silu(gate) in fp32; per group of group_size channels h *= 1/sqrt(mean(h^2) + eps);
+ * out = weight * (h rounded to io_dtype).  Replaces the NemotronH mixer's norm(y, gate)
+ * (transformers Zamba2RMSNormGated; scale/v4_native_decode.py:171, restated by the reference
+ * in scale/nemotron_retrofit.py:146-161).  y, gate, out: [batch][dim] in io_dtype (F32 /
+ * BF16); weight: [dim] in weight_dtype; group_size divides dim and is <= 2048. */
+NSSM_API int nssm_gated_rmsnorm(const void* y, int64_t y_stride, const void* gate, int64_t gate_stride,
+                                const void* weight, int32_t weight_dtype, float eps, int32_t batch,
+                                int32_t dim, int32_t group_size, int32_t io_dtype, void* out,
+                                int64_t out_stride, void* stream);
 
 /* Bytes of workspace nssm_tiered_step / nssm_fresh_step need for `batch` rows
  * when R != NULL (the rotated B and C), 0 otherwise. */

@@ -10,6 +10,7 @@ the host; the work runs in hand-written CUDA behind the C ABI of
 from ._lib import load as load_library, supported_hot_dims  # noqa: F401
 from .ops import (  # noqa: F401
     conv_step,
+    gated_rmsnorm,
     materialize,
     prefill_snapshot,
     prefill_split,

@@ -21,7 +21,7 @@ EXPORTED = (
     "nssm_step_workspace_bytes", "nssm_tiered_step", "nssm_fresh_step", "nssm_prefill_split",
     "nssm_materialize", "nssm_rot_flat", "nssm_supported_hot_dims", "nssm_sizeof_pool",
     "nssm_sizeof_step_args", "nssm_abi_version", "nssm_last_error", "nssm_tiered_step_static",
-    "nssm_conv_step", "nssm_sizeof_conv_args",
+    "nssm_conv_step", "nssm_sizeof_conv_args", "nssm_gated_rmsnorm",
 )
 
 
@@ -109,6 +109,7 @@ def load(auto_build: bool = True) -> C.CDLL:
             "nssm_tiered_step_static": (C.c_int, [P_pool, P_args, vp]),
             "nssm_conv_step": (C.c_int, [C.POINTER(NssmConvArgs), vp]),
             "nssm_sizeof_conv_args": (sz, []),
+            "nssm_gated_rmsnorm": (C.c_int, [vp, i64, vp, i64, vp, i32, C.c_float, i32, i32, i32, i32, vp, i64, vp]),
             "nssm_fresh_step": (C.c_int, [vp, i32, i32, i32, i32, i32, P_args, vp]),
             "nssm_prefill_split": (C.c_int, [P_pool, vp, i64, vp, i32, i32, vp]),
             "nssm_materialize": (C.c_int, [P_pool, vp, vp, i32, i32, vp, i64, vp]),

@@ -8,6 +8,7 @@
 #include <string>
 
 #include "nssm_host.cuh"
+#include "nssm_norm.cuh"
 
 namespace nssm_host {
 
@@ -366,6 +367,26 @@ int nssm_conv_step(const nssm_conv_args* a, void* stream) {
   }
   if (iobf) return wbf ? launch_conv<4, 4, true, true, false>(cp, B, G, st) : launch_conv<4, 4, true, false, false>(cp, B, G, st);
   return wbf ? launch_conv<4, 4, false, true, false>(cp, B, G, st) : launch_conv<4, 4, false, false, false>(cp, B, G, st);
+}
+
+int nssm_gated_rmsnorm(const void* y, int64_t y_stride, const void* gate, int64_t gate_stride, const void* weight,
+                       int32_t weight_dtype, float eps, int32_t batch, int32_t dim, int32_t group_size,
+                       int32_t io_dtype, void* out, int64_t out_stride, void* stream) {
+  if (batch < 0 || batch > 65535) return fail(NSSM_ERR_INVALID, "batch %d outside [0, 65535]", batch);
+  if (batch == 0) return NSSM_OK;
+  if (!y || !gate || !weight || !out) return fail(NSSM_ERR_INVALID, "y / gate / weight / out is NULL");
+  if (dim <= 0 || group_size <= 0 || dim % group_size || group_size > nssm::kNormThreads * nssm::kNormMaxPer)
+    return fail(NSSM_ERR_INVALID, "dim %d / group_size %d unsupported (group_size divides dim, <= %d)", dim,
+                group_size, nssm::kNormThreads * nssm::kNormMaxPer);
+  if (dim / group_size > 65535) return fail(NSSM_ERR_INVALID, "too many groups");
+  if ((io_dtype != NSSM_F32 && io_dtype != NSSM_BF16) || (weight_dtype != NSSM_F32 && weight_dtype != NSSM_BF16))
+    return fail(NSSM_ERR_INVALID, "dtypes must be F32 or BF16");
+  nssm::NormParams np{};
+  np.y = y; np.y_sb = y_stride; np.gate = gate; np.g_sb = gate_stride; np.weight = weight; np.w_dtype = weight_dtype;
+  np.eps = eps; np.dim = dim; np.gs = group_size; np.dtype = io_dtype; np.out = out; np.o_sb = out_stride;
+  dim3 grid((unsigned)(dim / group_size), (unsigned)batch);
+  nssm::gated_rmsnorm_kernel<<<grid, nssm::kNormThreads, 0, static_cast<cudaStream_t>(stream)>>>(np);
+  return cuda_check("gated_rmsnorm_kernel launch");
 }
 
 size_t nssm_sizeof_conv_args(void) { return sizeof(nssm_conv_args); }

@@ -6,7 +6,7 @@ prefill (or any call that is not a one-token decode with a cache) runs the model
 torch forward, after which the final recurrent state of every row is split into a tiered
 slot pool; each one-token decode then runs in_proj, ``conv_step`` (conv1d update of the HF
 cache's conv state, SiLU, split, rotation by the mixer's ``ActRotMask`` R when it has one),
-``tiered_state_update`` and the mixer's own gated norm and out_proj.  The decode path runs
+``tiered_state_update``, ``gated_rmsnorm`` (the mixer's norm) and out_proj.  The decode path runs
 on the GPU only; the model's weights and cache must live on a CUDA device.
 
 Cold storage: ``cold="fp32"`` reproduces the reference's ``cold_bf16=0`` to fp32 rounding;
@@ -17,7 +17,7 @@ from __future__ import annotations
 
 import torch
 
-from .ops import conv_step, prefill_split, tiered_state_update
+from .ops import conv_step, gated_rmsnorm, prefill_split, tiered_state_update
 from .pool import TieredSlotPool
 
 _MODES = {(0, 0): "stale", (1, 0): "corr", (0, 1): "coldoff"}
@@ -60,7 +60,11 @@ def _decode(self, input_states, cache_params):
     y = torch.empty(b, H, P, dtype=dtype, device=input_states.device)
     tiered_state_update(st["pool"], 0, x, dt[:, 0], A, Bv, Cv, self.D, self.dt_bias, True, st["slots"], -1, y,
                         None, self.time_step_min, st["mode"])
-    scan_output = self.norm(y.reshape(b, 1, I), gate)
+    norm = self.norm
+    if all(hasattr(norm, a) for a in ("weight", "variance_epsilon", "group_size")):   # Zamba2RMSNormGated
+        scan_output = gated_rmsnorm(y.reshape(b, 1, I), gate, norm.weight, norm.variance_epsilon, norm.group_size)
+    else:
+        scan_output = norm(y.reshape(b, 1, I), gate)
     return self.out_proj(scan_output.to(dtype))
 
 

@@ -325,3 +325,30 @@ def conv_step(xbc: torch.Tensor, conv_state: torch.Tensor, weight: torch.Tensor,
     keep = (xbc, conv_state, w, bias, idx, Rf, x_out, B_out, C_out, status)  # noqa: F841
     _lib.check(_lib.load().nssm_conv_step(C.byref(a), _stream(dev)))
     return x_out, B_out, C_out
+
+
+def gated_rmsnorm(y: torch.Tensor, gate: torch.Tensor, weight: torch.Tensor, eps: float, group_size: int,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """The NemotronH mixer's ``norm(y, gate)`` in one launch: ``h = y * silu(gate)``, per group
+    of ``group_size`` channels ``h / sqrt(mean(h^2) + eps)``, rounded to y's dtype, times
+    ``weight`` (transformers Zamba2RMSNormGated; scale/nemotron_retrofit.py:146-161).
+    ``y``, ``gate``: ``[..., dim]``; returns the same shape in y's dtype."""
+    shape = y.shape
+    dim = shape[-1]
+    y2 = y.reshape(-1, dim)
+    g2 = gate.reshape(-1, dim)
+    if y2.stride(-1) != 1 or g2.stride(-1) != 1:
+        raise ValueError("y and gate need a unit inner stride")
+    if y.dtype not in (torch.bfloat16, torch.float32) or gate.dtype != y.dtype:
+        raise ValueError("y and gate must share a bf16 / fp32 dtype")
+    w = weight if weight.is_contiguous() else weight.contiguous()
+    if w.numel() != dim or w.dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError(f"weight must have {dim} bf16 / fp32 entries")
+    dev = _require_cuda(y2, g2, w)
+    if out is None:
+        out = torch.empty(y2.shape, dtype=y.dtype, device=dev)
+    o2 = out.reshape(-1, dim)
+    _lib.check(_lib.load().nssm_gated_rmsnorm(y2.data_ptr(), y2.stride(0), g2.data_ptr(), g2.stride(0), w.data_ptr(),
+                                              nssm_dtype(w.dtype), float(eps), y2.shape[0], dim, int(group_size),
+                                              nssm_dtype(y.dtype), o2.data_ptr(), o2.stride(0), _stream(dev)))
+    return out.reshape(shape)

@@ -51,7 +51,7 @@ __all__ = [
     "FP8", "FP8_MAX", "SCALE_EPS", "rot_flat", "dt_softplus", "quantize_rows",
     "dequantize_rows", "TieredPoolRef", "NativePoolRef", "prefill_split",
     "tiered_step", "native_step", "fresh_step", "materialize", "make_inputs",
-    "make_params", "fp8_ordered_codes", "conv_step", "conv_split",
+    "make_params", "fp8_ordered_codes", "conv_step", "conv_split", "gated_rmsnorm",
 ]
 
 FP8 = torch.float8_e4m3fn
@@ -164,6 +164,21 @@ def conv_split(out: torch.Tensor, I: int, G: int, N: int, R: torch.Tensor | None
     if R is not None:
         Bv, Cv = rot_flat(Bv, R, "fp32"), rot_flat(Cv, R, "fp32")
     return x, Bv.reshape(b, G, N), Cv.reshape(b, G, N)
+
+
+def gated_rmsnorm(y: torch.Tensor, gate: torch.Tensor, weight: torch.Tensor, eps: float,
+                  group_size: int) -> torch.Tensor:
+    """The mixer's ``norm(y, gate)`` after the state op (scale/v4_native_decode.py:171):
+    transformers' Zamba2RMSNormGated, restated by the reference as
+    ``rmsnorm_fn(norm_before_gate=False)`` (scale/nemotron_retrofit.py:146-161):
+    ``h = y * silu(gate)`` in fp32, per group ``h * rsqrt(mean(h^2) + eps)``, cast to y's
+    dtype, times ``weight``."""
+    dt = y.dtype
+    h = y.float() * F.silu(gate.float())
+    s = h.shape
+    hg = h.view(*s[:-1], s[-1] // group_size, group_size)
+    hg = hg * torch.rsqrt(hg.pow(2).mean(-1, keepdim=True) + eps)
+    return (weight * hg.view(s).to(dt)).to(dt)
 
 
 # --------------------------------------------------------------------------

@@ -122,6 +122,11 @@ __device__ __forceinline__ float div_rn_fma(float a, float b, float r) {
   const float e = __fmaf_rn(-q0, b, a);
   return __fmaf_rn(e, r, q0);
 }
+// amax / 448 correctly rounded: Markstein's correction with rn(1/448); quotients far below
+// the normal range (amax < 2^-100) take the full division
+__device__ __forceinline__ float scale_div448(float m) {
+  return m >= 0x1p-100f ? div_rn_fma(m, kFp8Max, 1.0f / kFp8Max) : __fdiv_rn(m, kFp8Max);
+}
 
 // Byte layout of the dynamic shared memory (computed on the host, passed in).
 struct PLayout {
@@ -673,10 +678,10 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
       // each into one multiply (below), which moves a stored code by one step, rarely.
       const float A_h = sA[h];
       const bool pre = c <= kRingF32Max;
-      if (pre) {
-        const float* fs = reinterpret_cast<const float*>(sm + L.off_fsc) + (b * H + h - beg) * (2 * c + 1);
-        for (int e = lane; e < 2 * c + 1; e += 32) wsc[e] = fs[e];
-      } else if (lane == 0) {   // suffix decays (per warp; identical in every warp)
+      // exp(suf_j) [c], dt_j [c], exp(total): the prologue's table, or computed per warp
+      const float* dec = pre ? reinterpret_cast<const float*>(sm + L.off_fsc) + (b * H + h - beg) * (2 * c + 1)
+                             : wsc;
+      if (!pre && lane == 0) {   // suffix decays (per warp; identical in every warp)
         float tot = 0.0f;
         for (int j = 0; j < c; ++j) tot = tot + ring_dt_at(j) * A_h;
         wsc[2 * c] = expf(tot);
@@ -689,13 +694,13 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
           wsc[c + j] = ring_dt_at(j);
         }
       }
-      __syncwarp();
+      if (!pre) __syncwarp();
       // W_j[row] = exp(suf_j) * (dt_j * x_j[row]) for the band's rows
       for (int j = 0; j < c; ++j) {
-        if (lane < nrow) sW[j * Pn + r0 + lane] = __fmul_rn(wsc[j], __fmul_rn(wsc[c + j], ring_x_at(j, r0 + lane)));
+        if (lane < nrow) sW[j * Pn + r0 + lane] = __fmul_rn(dec[j], __fmul_rn(dec[c + j], ring_x_at(j, r0 + lane)));
       }
       __syncwarp();
-      const float etot = wsc[2 * c];
+      const float etot = dec[2 * c];
       const float* scl_s = reinterpret_cast<const float*>(st + L.s_scale);
       const float* rbp = ring_st ? reinterpret_cast<const float*>(st + L.s_rb)
                                  : p.ring_b + ((int64_t)slot * p.G + g) * c * NC;
@@ -765,7 +770,7 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
           float m = 0.0f;
 #pragma unroll
           for (int k = 0; k < CPR; ++k) m = fmaxf(m, pc[row * CPR + k]);
-          const float sc = __fadd_rn(__fdiv_rn(m, kFp8Max), kScaleEps);
+          const float sc = __fadd_rn(scale_div448(m), kScaleEps);
           s_sc[row] = sc;
           s_rcp[row] = __frcp_rn(sc);
           p.scale[sh * Pn + row] = sc;
@@ -851,7 +856,7 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
             float m = 0.0f;
   #pragma unroll
             for (int cc = 0; cc < CPR; ++cc) m = fmaxf(m, pc[row * CPR + cc]);
-            const float sc = __fadd_rn(__fdiv_rn(m, kFp8Max), kScaleEps);
+            const float sc = __fadd_rn(scale_div448(m), kScaleEps);
             s_sc[row] = sc;
             s_rcp[row] = __frcp_rn(sc);
             p.scale[sh * Pn + row] = sc;

@@ -201,17 +201,6 @@ struct PParams {
 
 __device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
 
-// e4m3 byte s|eeee|mmm placed at f32 bits 31|26..23|22..20 is exactly q * 2^-120,
-// subnormals and zero included (the f32 exponent field 0000eeee is the e4m3 one
-// re-biased by 120): four values per word from integer shifts and masks only.
-constexpr float kTwo120 = 1.329227995784915872903807060280344576e36f;   // 2^120
-__device__ __forceinline__ void fp8x4_scaled(uint32_t w, float* v) {
-  v[0] = __int_as_float((static_cast<int>(w << 24) >> 4) & static_cast<int>(0x87F00000u));
-  v[1] = __int_as_float((static_cast<int>(w << 16) >> 4) & static_cast<int>(0x87F00000u));
-  v[2] = __int_as_float((static_cast<int>(w << 8) >> 4) & static_cast<int>(0x87F00000u));
-  v[3] = __int_as_float((static_cast<int>(w) >> 4) & static_cast<int>(0x87F00000u));
-}
-
 template <bool IOBF>
 __device__ __forceinline__ float ldv(const void* p, int64_t i) {
   if constexpr (IOBF) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);

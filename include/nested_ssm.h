@@ -39,6 +39,11 @@
  *        state the native path keeps in cache (scale/v4_native_decode.py:65-67).
  *  - nssm_gated_rmsnorm: the mixer's norm(y, gate) after the state op
  *        (scale/v4_native_decode.py:171; scale/nemotron_retrofit.py:146-161).
+ *  - nssm_chunk_scan   : the prefill chunked scan of the lean prefill
+ *        (scale/v4_native_decode.py:175-220), i.e. mamba_ssm's
+ *        mamba_chunk_scan_combined (called at scale/v4_native_decode.py:209-216)
+ *        with z = NULL and the final states returned; its final state feeds
+ *        nssm_prefill_split.
  *  - nssm_conv_step    : causal_conv1d_update + split + the post-conv R rotation of
  *        _v4_fused_decode (scale/v4_fused_decode.py:39-48); the HF decode branch's
  *        conv-state roll + weighted sum + act (scale/v4_native_decode.py:36-49).
@@ -187,6 +192,46 @@ NSSM_API int nssm_gated_rmsnorm(const void* y, int64_t y_stride, const void* gat
                                 const void* weight, int32_t weight_dtype, float eps, int32_t batch,
                                 int32_t dim, int32_t group_size, int32_t io_dtype, void* out,
                                 int64_t out_stride, void* stream);
+
+/* Prefill chunked scan of one layer (the SSD chunk scan of mamba_ssm 2.3.2.post1
+ * mamba_chunk_scan_combined with z = NULL and return_final_states; the reference's lean
+ * prefill, scale/v4_native_decode.py:209-216).  Per (sequence, head), chunks of chunk_size
+ * tokens: dt = clamp(softplus(dt + dt_bias), dt_min, dt_max) (softplus only if dt_softplus),
+ * dA_cs = cumsum(dt * A) inside the chunk, y = C.S_prev * exp(dA_cs) + sum_{s<=l} M x_s + D x
+ * with M = bf16(C_l.B_s exp(dA_cs_l - dA_cs_s) dt_s), S_chunk = sum_s x_s bf16(B_s
+ * exp(dA_cs_last - dA_cs_s) dt_s), S = exp(dA_cs_last) S + S_chunk (fp32; S_prev is S entering
+ * the chunk rounded to bf16).  x, B, C, y in bf16 with fp32 accumulation on the tensor cores;
+ * head h uses group h / (nheads / ngroups).  Compiled for chunk_size 128, dstate 128 and
+ * headdim 64 or 80.  Strides in elements; x / B / C / y 16-byte aligned with strides that are
+ * multiples of 8. */
+typedef struct {
+  int32_t batch, seqlen, nheads, headdim, ngroups, dstate, chunk_size;
+  int32_t io_dtype;       /* BF16                                                   */
+  const void* x;          /* [batch][seqlen][nheads][headdim]                       */
+  int64_t x_stride_b, x_stride_t;
+  const void* dt;         /* [batch][seqlen][nheads], before dt_bias / softplus     */
+  int64_t dt_stride_b, dt_stride_t;
+  int32_t dt_dtype;       /* F32 or BF16                                            */
+  int32_t dt_softplus;
+  float dt_min, dt_max;   /* dt_limit; (0, +inf) is no clamp                         */
+  const float* A;         /* [nheads] (negative)                                    */
+  const float* D;         /* [nheads] or NULL                                       */
+  const float* dt_bias;   /* [nheads] or NULL                                       */
+  const void* B;          /* [batch][seqlen][ngroups][dstate]                       */
+  int64_t B_stride_b, B_stride_t;
+  const void* C;
+  int64_t C_stride_b, C_stride_t;
+  const float* initial_states; /* [batch][nheads][headdim][dstate] fp32 or NULL     */
+  int64_t init_stride_b;
+  void* y;                /* [batch][seqlen][nheads][headdim] bf16                  */
+  int64_t y_stride_b, y_stride_t;
+  float* final_states;    /* [batch][nheads][headdim][dstate] fp32 or NULL          */
+  int64_t final_stride_b;
+  int32_t* status;        /* optional device word, bit 1 = a tensor-core wait timed out */
+} nssm_scan_args;
+
+NSSM_API int nssm_chunk_scan(const nssm_scan_args* args, void* stream);
+NSSM_API size_t nssm_sizeof_scan_args(void);
 
 /* Bytes of workspace nssm_tiered_step / nssm_fresh_step need for `batch` rows
  * when R != NULL (the rotated B and C), 0 otherwise. */

@@ -11,6 +11,7 @@ from ._lib import load as load_library, supported_hot_dims  # noqa: F401
 from .ops import (  # noqa: F401
     conv_step,
     gated_rmsnorm,
+    mamba_chunk_scan_combined,
     materialize,
     prefill_snapshot,
     prefill_split,

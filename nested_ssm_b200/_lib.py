@@ -21,7 +21,8 @@ EXPORTED = (
     "nssm_step_workspace_bytes", "nssm_tiered_step", "nssm_fresh_step", "nssm_prefill_split",
     "nssm_materialize", "nssm_rot_flat", "nssm_supported_hot_dims", "nssm_sizeof_pool",
     "nssm_sizeof_step_args", "nssm_abi_version", "nssm_last_error", "nssm_tiered_step_static",
-    "nssm_conv_step", "nssm_sizeof_conv_args", "nssm_gated_rmsnorm",
+    "nssm_conv_step", "nssm_sizeof_conv_args", "nssm_gated_rmsnorm", "nssm_chunk_scan",
+    "nssm_sizeof_scan_args",
 )
 
 
@@ -74,6 +75,23 @@ class NssmConvArgs(C.Structure):
     ]
 
 
+class NssmScanArgs(C.Structure):
+    _fields_ = [
+        ("batch", C.c_int32), ("seqlen", C.c_int32), ("nheads", C.c_int32), ("headdim", C.c_int32),
+        ("ngroups", C.c_int32), ("dstate", C.c_int32), ("chunk_size", C.c_int32), ("io_dtype", C.c_int32),
+        ("x", C.c_void_p), ("x_stride_b", C.c_int64), ("x_stride_t", C.c_int64),
+        ("dt", C.c_void_p), ("dt_stride_b", C.c_int64), ("dt_stride_t", C.c_int64),
+        ("dt_dtype", C.c_int32), ("dt_softplus", C.c_int32), ("dt_min", C.c_float), ("dt_max", C.c_float),
+        ("A", C.c_void_p), ("D", C.c_void_p), ("dt_bias", C.c_void_p),
+        ("B", C.c_void_p), ("B_stride_b", C.c_int64), ("B_stride_t", C.c_int64),
+        ("C", C.c_void_p), ("C_stride_b", C.c_int64), ("C_stride_t", C.c_int64),
+        ("initial_states", C.c_void_p), ("init_stride_b", C.c_int64),
+        ("y", C.c_void_p), ("y_stride_b", C.c_int64), ("y_stride_t", C.c_int64),
+        ("final_states", C.c_void_p), ("final_stride_b", C.c_int64),
+        ("status", C.c_void_p),
+    ]
+
+
 _lib = None
 _lock = threading.Lock()
 
@@ -109,6 +127,8 @@ def load(auto_build: bool = True) -> C.CDLL:
             "nssm_tiered_step_static": (C.c_int, [P_pool, P_args, vp]),
             "nssm_conv_step": (C.c_int, [C.POINTER(NssmConvArgs), vp]),
             "nssm_sizeof_conv_args": (sz, []),
+            "nssm_chunk_scan": (C.c_int, [C.POINTER(NssmScanArgs), vp]),
+            "nssm_sizeof_scan_args": (sz, []),
             "nssm_gated_rmsnorm": (C.c_int, [vp, i64, vp, i64, vp, i32, C.c_float, i32, i32, i32, i32, vp, i64, vp]),
             "nssm_fresh_step": (C.c_int, [vp, i32, i32, i32, i32, i32, P_args, vp]),
             "nssm_prefill_split": (C.c_int, [P_pool, vp, i64, vp, i32, i32, vp]),
@@ -126,7 +146,8 @@ def load(auto_build: bool = True) -> C.CDLL:
         if lib.nssm_abi_version() != ABI_VERSION:
             raise RuntimeError(f"libnested_ssm ABI {lib.nssm_abi_version()} != binding {ABI_VERSION}")
         if (lib.nssm_sizeof_pool() != C.sizeof(NssmPool) or lib.nssm_sizeof_step_args() != C.sizeof(NssmStepArgs)
-                or lib.nssm_sizeof_conv_args() != C.sizeof(NssmConvArgs)):
+                or lib.nssm_sizeof_conv_args() != C.sizeof(NssmConvArgs)
+                or lib.nssm_sizeof_scan_args() != C.sizeof(NssmScanArgs)):
             raise RuntimeError("libnested_ssm struct layout differs from the ctypes binding")
         _lib = lib
         return lib

@@ -19,7 +19,7 @@ INCLUDE = os.path.join(REPO_DIR, "include")
 LIB_NAME = "libnested_ssm.so"
 LIB_PATH = os.path.join(PKG_DIR, LIB_NAME)
 
-SOURCES = ["nssm_abi.cu", "nssm_pb16.cu", "nssm_pb32.cu", "nssm_pb64.cu", "nssm_static.cu"]
+SOURCES = ["nssm_abi.cu", "nssm_pb16.cu", "nssm_pb32.cu", "nssm_pb64.cu", "nssm_static.cu", "nssm_scan.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -9,6 +9,9 @@
 * :func:`prefill_snapshot` / :func:`prefill_split` -- scale/vllm_v4_patch.py:123-137.
 * :func:`rot_flat` -- scale/vllm_v4_patch.py:41-45 (fp32 accumulation, cast back).
 * :func:`materialize` -- exact full fp32 state of slots (read-only).
+* :func:`mamba_chunk_scan_combined` -- the prefill chunked scan of the lean prefill
+  (scale/v4_native_decode.py:209-216), mamba_ssm's argument order; its final states feed
+  :func:`prefill_split`.
 
 All tensors must live on the same CUDA device; work is enqueued on the current
 stream and never synchronised.  There is no CPU fallback.
@@ -352,3 +355,72 @@ def gated_rmsnorm(y: torch.Tensor, gate: torch.Tensor, weight: torch.Tensor, eps
                                               nssm_dtype(w.dtype), float(eps), y2.shape[0], dim, int(group_size),
                                               nssm_dtype(y.dtype), o2.data_ptr(), o2.stride(0), _stream(dev)))
     return out.reshape(shape)
+
+
+def mamba_chunk_scan_combined(x, dt, A, B, C_, chunk_size, D=None, z=None, dt_bias=None, initial_states=None,
+                              seq_idx=None, cu_seqlens=None, dt_softplus=False, dt_limit=(0.0, float("inf")),
+                              return_final_states=False, *, out=None, final_states=None, status=None):
+    """Prefill chunked scan of one layer with mamba_ssm's call surface (as the reference's
+    lean prefill makes it, scale/v4_native_decode.py:209-216): ``x [b, T, H, P]``,
+    ``dt [b, T, H]`` (before bias and softplus), ``A [H]``, ``B``/``C_ [b, T, G, N]`` in bf16,
+    ``D``/``dt_bias [H]``, ``initial_states [b, H, P, N]`` or None.  Returns ``y [b, T, H, P]``
+    (bf16), and with ``return_final_states`` also the fp32 ``[b, H, P, N]`` final states.
+    ``z``, ``seq_idx`` and ``cu_seqlens`` are not supported (the reference passes none)."""
+    if z is not None or seq_idx is not None or cu_seqlens is not None:
+        raise NotImplementedError("z / seq_idx / cu_seqlens are not supported by the chunk scan")
+    if x.dim() != 4 or dt.dim() != 3 or B.dim() != 4 or C_.dim() != 4:
+        raise ValueError("x [b, T, H, P], dt [b, T, H], B / C [b, T, G, N] expected")
+    b, T, H, P = x.shape
+    G, N = B.shape[2], B.shape[3]
+    if dt.shape != (b, T, H) or B.shape != (b, T, G, N) or C_.shape != (b, T, G, N):
+        raise ValueError(f"shape mismatch: x {tuple(x.shape)} dt {tuple(dt.shape)} B {tuple(B.shape)} "
+                         f"C {tuple(C_.shape)}")
+    if x.dtype != torch.bfloat16 or B.dtype != torch.bfloat16 or C_.dtype != torch.bfloat16:
+        raise ValueError("x, B and C must be bf16")
+    if dt.dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError("dt must be bf16 or fp32")
+    if D is not None and D.dim() > 1:
+        raise NotImplementedError("D with a headdim axis is not supported (D must be [H])")
+
+    def rows(t, inner):   # unit innermost stride and packed inner dims
+        if t.stride(-1) != 1 or (t.dim() == 4 and t.stride(2) != inner):
+            t = t.contiguous()
+        return t
+
+    x, B, C_ = rows(x, P), rows(B, N), rows(C_, N)
+    if dt.stride(-1) != 1:
+        dt = dt.contiguous()
+    Af, Df, bf = _per_head(A, H, "A"), _per_head(D, H, "D"), _per_head(dt_bias, H, "dt_bias")
+    init = None
+    if initial_states is not None:
+        if initial_states.shape != (b, H, P, N):
+            raise ValueError(f"initial_states must be [{b}, {H}, {P}, {N}]")
+        init = initial_states.float().contiguous()
+    dev = _require_cuda(x, dt, Af, B, C_, Df, bf, init)
+    if out is None:
+        out = torch.empty(b, T, H, P, dtype=torch.bfloat16, device=dev)
+    if out.shape != (b, T, H, P) or out.dtype != torch.bfloat16 or out.stride(-1) != 1 or out.stride(2) != P:
+        raise ValueError("out must be bf16 [b, T, H, P] with packed (H, P)")
+    if return_final_states and final_states is None:
+        final_states = torch.empty(b, H, P, N, dtype=torch.float32, device=dev)
+    if final_states is not None and (final_states.shape != (b, H, P, N) or final_states.dtype != torch.float32
+                                     or not final_states[0].is_contiguous()):
+        raise ValueError("final_states must be fp32 [b, H, P, N] with contiguous rows")
+    a = _lib.NssmScanArgs()
+    a.batch, a.seqlen, a.nheads, a.headdim, a.ngroups, a.dstate = b, T, H, P, G, N
+    a.chunk_size, a.io_dtype = int(chunk_size), _lib.NSSM_BF16
+    a.x, a.x_stride_b, a.x_stride_t = x.data_ptr(), x.stride(0), x.stride(1)
+    a.dt, a.dt_stride_b, a.dt_stride_t = dt.data_ptr(), dt.stride(0), dt.stride(1)
+    a.dt_dtype, a.dt_softplus = nssm_dtype(dt.dtype), int(bool(dt_softplus))
+    a.dt_min, a.dt_max = float(dt_limit[0]), float(dt_limit[1])
+    a.A, a.D, a.dt_bias = Af.data_ptr(), _ptr(Df), _ptr(bf)
+    a.B, a.B_stride_b, a.B_stride_t = B.data_ptr(), B.stride(0), B.stride(1)
+    a.C, a.C_stride_b, a.C_stride_t = C_.data_ptr(), C_.stride(0), C_.stride(1)
+    a.initial_states, a.init_stride_b = _ptr(init), (H * P * N)
+    a.y, a.y_stride_b, a.y_stride_t = out.data_ptr(), out.stride(0), out.stride(1)
+    a.final_states = _ptr(final_states)
+    a.final_stride_b = final_states.stride(0) if final_states is not None else 0
+    a.status = _ptr(status)
+    keep = (x, dt, Af, B, C_, Df, bf, init, out, final_states, status)  # noqa: F841
+    _lib.check(_lib.load().nssm_chunk_scan(C.byref(a), _stream(dev)))
+    return (out, final_states) if return_final_states else out

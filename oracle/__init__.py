@@ -14,3 +14,4 @@ outputs as fixtures; ``tests/test_oracle_golden.py`` checks this oracle
 against them.
 """
 from .tiered import *  # noqa: F401,F403
+from .scan import *  # noqa: F401,F403

@@ -23,6 +23,16 @@ regenerate (checksums stored beside the outputs):
   a conv state advanced by the transformers cache roll) and the reference's own
   ``ActRotMask`` (``scale/nemotron_retrofit.py:18-54``: SiLU, then the rotation of B and C)
   as the activation, so y covers conv + SiLU + split + rotation + tiered state op.
+* ``prefill_hf.npz`` -- the reference's prefill dispatch (``_dispatch`` of
+  ``scale/v4_native_decode.py:223-244`` with ``lean_prefill=0``, i.e. transformers' NemotronH
+  ``torch_forward`` chunked SSD prefill) on a stub mixer whose in_proj, act, norm and
+  out_proj are identities and whose conv1d is a causal identity, so its inputs are the seeded
+  (x, B, C, dt_raw) of a 100-token prompt (one ragged chunk of the 128-token chunking) and
+  its outputs are the pre-norm y and the final recurrent state the tiered pool is split from.
+  One chunk only: transformers 5.5's ``torch_forward`` sums its chunk-decay matrix over the
+  wrong index, so for prompts longer than a chunk its carried state is not the recurrence's
+  (its final state is the last chunk's local state); the reference's default prefill
+  (``lean_prefill=1``, mamba_ssm's ``mamba_chunk_scan_combined``) has no such step.
 * ``hf_generate.npz`` -- the reference's HF integration end to end: a small random NemotronH
   (two Mamba2 layers and one attention layer, seeded), its mixers' activation wrapped in the
   reference's ``ActRotMask`` with seeded rotations, ``install(model, pb=32, c=4,
@@ -52,6 +62,7 @@ VLLM = dict(b=2, S=4, H=8, P=80, N=128, G=2, pb=32, c=4, seed=12, steps=9, slots
 ROT = dict(T=6, G=2, N=128, seed=13)
 CONV = dict(b=2, H=16, P=80, N=128, G=2, pb=32, c=4, seed=14, steps=9, K=4)
 HF = dict(b=2, prompt=7, new=9, seed=15, pb=32, c=4)
+PREFILL = dict(b=2, T=100, H=4, P=80, N=128, G=2, chunk=128, seed=16)
 
 
 def hf_model(seed: int):
@@ -283,6 +294,56 @@ def make_native_conv(ref):
     return arrays
 
 
+def prefill_inputs(cfg):
+    """Seeded prefill inputs, bf16-representable values held in fp32: x ~ N(0,1),
+    B, C ~ N(0,1) / N**0.25 (so C.B is O(1)), dt_raw ~ N(0,1); A, D, dt_bias of make_params."""
+    b, T, H, P, N, G, seed = (cfg[k] for k in ("b", "T", "H", "P", "N", "G", "seed"))
+    prm = O.make_params(H, G, N, seed=seed)[0]
+    g = torch.Generator().manual_seed(seed + 200)
+    bf = lambda t: t.to(torch.bfloat16).float()   # noqa: E731
+    return dict(x=bf(torch.randn(b, T, H, P, generator=g)),
+                B=bf(torch.randn(b, T, G, N, generator=g) / N ** 0.25),
+                C=bf(torch.randn(b, T, G, N, generator=g) / N ** 0.25),
+                dt=bf(torch.randn(b, T, H, generator=g)),
+                A=-torch.exp(torch.log(-prm["A"]).float()), D=prm["D"], dt_bias=prm["dt_bias"],
+                A_log=torch.log(-prm["A"]))
+
+
+def make_prefill(ref):
+    sys.path.insert(0, os.path.join(ref, "scale"))
+    import v4_native_decode as V
+    cfg = PREFILL
+    b, T, H, P, N, G, Q = (cfg[k] for k in ("b", "T", "H", "P", "N", "G", "chunk"))
+    inp = prefill_inputs(cfg)
+    K = 4
+    I, conv_dim = H * P, H * P + 2 * G * N
+    conv = torch.nn.Conv1d(conv_dim, conv_dim, K, groups=conv_dim, padding=K - 1, bias=False)
+    conv.weight.data.zero_()
+    conv.weight.data[:, 0, -1] = 1.0                   # causal identity
+    m = types.SimpleNamespace(
+        num_heads=H, head_dim=P, ssm_state_size=N, n_groups=G, intermediate_size=I, conv_dim=conv_dim,
+        conv_kernel_size=K, chunk_size=Q, in_proj=torch.nn.Identity(), act=torch.nn.Identity(), conv1d=conv,
+        use_conv_bias=False, A_log=inp["A_log"], D=inp["D"], dt_bias=inp["dt_bias"], time_step_min=1e-3,
+        time_step_limit=(0.0, float("inf")), layer_idx=0, out_proj=torch.nn.Identity(),
+        norm=lambda y, gate: y, _v4state=None, v4cfg=dict(pb=32, c=4, cold_bf16=0, lean_prefill=0))
+    cache = types.SimpleNamespace(layers=[types.SimpleNamespace(recurrent_states=None)])
+    cache.has_previous_state = lambda idx: False
+    cache.update_conv_state = lambda st, idx: st
+
+    def update_recurrent_state(s, idx):
+        cache.layers[idx].recurrent_states = s
+        return s
+
+    cache.update_recurrent_state = update_recurrent_state
+    proj = torch.cat([torch.zeros(b, T, I), inp["x"].reshape(b, T, I), inp["B"].reshape(b, T, G * N),
+                      inp["C"].reshape(b, T, G * N), inp["dt"]], dim=-1)
+    y = V._dispatch(m, proj, cache, None)
+    out = dict(y=y.reshape(b, T, H, P).float(), state=cache.layers[0].recurrent_states.float())
+    for k in ("x", "B", "C", "dt"):
+        out[f"sum_{k}"] = torch.tensor(checksum(inp[k]), dtype=torch.float64)
+    return out
+
+
 def make_hf(ref):
     sys.path.insert(0, os.path.join(ref, "scale"))
     import v4_native_decode as V
@@ -323,6 +384,7 @@ def main():
         save("rot_flat.npz", make_rot(a.reference))
         save("native_decode_conv.npz", make_native_conv(a.reference))
         save("hf_generate.npz", make_hf(a.reference))
+        save("prefill_hf.npz", make_prefill(a.reference))
 
 
 if __name__ == "__main__":

@@ -55,6 +55,12 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--cpu-sample-batch", type=int, default=4)
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of replaying CUDA graphs")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the prefill chunked-scan measurement")
+    ap.add_argument("--prefill-only", action="store_true",
+                    help="run only the prefill chunked-scan leg and print its JSON (profiling)")
+    ap.add_argument("--prefill-batch", type=int, default=64)
+    ap.add_argument("--prefill-len", type=int, default=2048)
+    ap.add_argument("--prefill-reps", type=int, default=0, help="timed launches (0: from --steps)")
     return ap.parse_args()
 
 
@@ -94,6 +100,14 @@ def load_peaks():
             d = json.load(f)
         return float(d["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+def load_tensor_peak() -> float:
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return float(json.load(f)["bf16_tflops"])
+    return 1590.0
 
 
 def load_traffic():
@@ -374,6 +388,81 @@ def time_conv(args, rank: int, ws: int):
             "kernel": "conv_step_kernel (conv1d update + SiLU + split + rotation of B and C)"}
 
 
+def prefill_bytes_per_token(io_bytes=2, dt_bytes=2) -> int:
+    """Algorithmic HBM bytes of the chunked scan per token-layer: x, B, C, dt in, y out (the
+    final state, H*P*N*4 per sequence, is added per launch)."""
+    return H * P * io_bytes + 2 * G * N * io_bytes + H * dt_bytes + H * P * io_bytes
+
+
+def prefill_flops_per_chunk(Q=128) -> int:
+    """Tensor-core FLOPs of one 128-token chunk of one sequence (mamba_ssm's algorithm:
+    C.B^T once per group; C.S_prev, M.x and the chunk state B_s^T.x per head)."""
+    return G * 2 * Q * Q * N + H * 3 * 2 * Q * N * P
+
+
+def time_prefill(args, rank: int, ws: int):
+    """nssm_chunk_scan (one layer's prefill scan, tcgen05) on a [batch, len] prompt batch: x, B,
+    C as views of one conv output and dt of one in_proj slice (the reference's layout), y and
+    the fp32 final states written; inputs and outputs larger than L2."""
+    from nested_ssm_b200 import mamba_chunk_scan_combined
+    dev = torch.device("cuda")
+    Bp, T = args.prefill_batch, args.prefill_len
+    I, GN = H * P, G * N
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4000 + rank)
+    xbc = torch.empty(Bp, T, I + 2 * GN, dtype=torch.bfloat16, device=dev)
+    xbc[..., :I].normal_(generator=gen)
+    xbc[..., I:].normal_(std=N ** -0.25, generator=gen)
+    dt = torch.randn(Bp, T, H, device=dev, generator=gen).to(torch.bfloat16)
+    A = -torch.exp(torch.rand(H, device=dev, generator=gen) * math.log(16.0))
+    D = torch.randn(H, device=dev, generator=gen)
+    dt_bias = torch.log(torch.expm1(torch.rand(H, device=dev, generator=gen) * (0.1 - 1e-3) + 1e-3))
+    x = xbc[..., :I].view(Bp, T, H, P)
+    Bv = xbc[..., I:I + GN].view(Bp, T, G, N)
+    Cv = xbc[..., I + GN:].view(Bp, T, G, N)
+    y = torch.empty(Bp, T, H, P, dtype=torch.bfloat16, device=dev)
+    fin = torch.empty(Bp, H, P, N, dtype=torch.float32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def run():
+        mamba_chunk_scan_combined(x, dt, A, Bv, Cv, 128, D=D, dt_bias=dt_bias, dt_softplus=True, out=y,
+                                  final_states=fin, status=status)
+
+    for _ in range(3):
+        run()
+    barrier(ws)
+    torch.cuda.synchronize()
+    reps = args.prefill_reps or max(3, args.steps // 8)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    if int(status.item()) != 0:
+        raise RuntimeError(f"chunk scan reported status {int(status.item())}")
+    ms = max_over_ranks(e0.elapsed_time(e1) / reps, ws)
+    barrier(ws)
+    del xbc, y, fin
+    torch.cuda.empty_cache()
+    peak, kind = load_peaks()
+    tflops_peak = load_tensor_peak()
+    nbytes = Bp * T * prefill_bytes_per_token() + Bp * H * P * N * 4
+    flops = Bp * ((T + 127) // 128) * prefill_flops_per_chunk()
+    gbs = nbytes / (ms / 1e3) / 1e9
+    tfs = flops / (ms / 1e3) / 1e12
+    return {"ms_per_launch": round(ms, 4), "tokens_per_s_per_layer": round(Bp * T / (ms / 1e3), 1),
+            "tokens_per_s_27_layers": round(Bp * T / (27 * ms / 1e3), 1),
+            "config": {"batch_per_gpu": Bp, "seqlen": T, "chunk_size": 128, "H": H, "P": P, "N": N, "G": G,
+                       "dtype": "bf16 x/B/C/y, fp32 accumulate and state", "layout": "x/B/C views of conv output"},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(gbs / peak, 4), "peak_kind": kind, "bytes_per_launch": nbytes,
+                         "tensor_tflops": round(tfs, 1), "tensor_frac": round(tfs / tflops_peak, 4),
+                         "flops_per_launch": flops},
+            "gpu_launches_per_layer": 1,
+            "kernel": "chunk_scan_kernel (tcgen05: C.B^T, C.S_prev, M.x, B_s^T.x per 128-token chunk)"}
+
+
 def time_e2e(wl: Workload, args, ws: int):
     """Same metric through the public API with HOST buffers: every step copies that
     step's inputs (x, dt, B, C of all layers) from pinned host memory and reads y
@@ -517,6 +606,14 @@ def main():
     if not torch.cuda.is_available():
         raise SystemExit("bench.py needs a CUDA device")
     import nested_ssm_b200  # noqa: F401  (fails loudly if the library is missing)
+    if args.prefill_only:
+        pf = time_prefill(args, rank, ws)
+        if rank == 0:
+            print(json.dumps({"prefill_scan": pf}), flush=True)
+        if ws > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return 0
     wl = Workload(args, rank)
     L, B, K, W = wl.L, wl.B, args.steps, max(3, args.warmup)
 
@@ -601,6 +698,7 @@ def main():
     torch.cuda.empty_cache()
     fresh = None if args.no_fresh else time_fresh(args, rank, ws)
     conv = None if args.no_conv else time_conv(args, rank, ws)
+    prefill = None if args.no_prefill else time_prefill(args, rank, ws)
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu:
@@ -625,6 +723,7 @@ def main():
             "fresh_control": fresh,
             "speedup_vs_fresh": round(value / fresh["tokens_per_s"], 3) if fresh else None,
             "conv_step": conv,
+            "prefill_scan": prefill,
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)

@@ -1,38 +1,46 @@
-// Prefill chunked scan (SSD) on the 5th-generation tensor cores.
+// Prefill chunked scan (SSD) on the 5th-generation tensor cores, warp-specialised.
 //
-// One CTA owns one (sequence, head) and walks its chunks of kQ = 128 tokens in order,
-// carrying the fp32 state S[P][N] in registers between chunks.  Per chunk, with
-// dA_cs = cumsum(dt * A) inside the chunk (the published algorithm of mamba_ssm 2.3.2.post1
-// mamba_chunk_scan_combined, which the reference's lean prefill calls at
+// Work item = one (sequence, head); a persistent CTA walks items blockIdx.x, +gridDim.x, ...
+// and each item's chunks of kQ = 128 tokens in order, as one stream of iterations.  Per
+// chunk, with cs = cumsum(dt * A) inside the chunk (the published algorithm of mamba_ssm
+// 2.3.2.post1 mamba_chunk_scan_combined, which the reference's lean prefill calls at
 // scale/v4_native_decode.py:209-216):
 //
 //   MMA1  CB[l][s]    = sum_n C[l][n] B[s][n]                       M=128 N=128 K=128
 //   MMA3  Yoff[l][p]  = sum_n C[l][n] Sprev[p][n]   (Sprev: bf16)   M=128 N=P   K=128
-//   --- CUDA cores: M[l][s] = bf16((CB * exp(cs_l - cs_s)) * dt_s) for s <= l, else 0;
-//                  B in place -> bf16(B[s][n] * exp(cs_last - cs_s) * dt_s)
+//   A     M[l][s] = bf16((CB * exp(cs_l - cs_s)) * dt_s) for s <= l, else 0;
+//         B in place -> bf16(B[s][n] * exp(cs_last - cs_s) * dt_s)
+//   MMA4  S[n][p]    += sum_s Bs[s][n] x[s][p]                      M=128 N=P   K=128
 //   MMA2  Ydiag[l][p] = sum_s M[l][s] x[s][p]                       M=128 N=P   K=128
-//   MMA4  Sc[n][p]    = sum_s Bs[s][n] x[s][p]                      M=128 N=P   K=128
-//   --- CUDA cores: y = Yoff * exp(cs_l) + Ydiag + D x  (rows l, warps 0-3)
-//                  S = exp(cs_last) S + Sc; Sprev = bf16(S)  (rows n, warps 4-7)
+//   E     S (fp32, tensor memory) <- exp(cs_last) S before MMA4 accumulates into it;
+//         Sprev = bf16(S); y = Yoff * exp(cs_l) + Ydiag + D x
 //
-// Accumulators live in tensor memory (512 columns: CB | Yoff | Ydiag | Sc), operands in
-// shared memory in the no-swizzle canonical layouts of tcgen05 descriptors (8-row x
-// 16-byte core matrices).  Loads are 16-byte cp.async into the next chunk's buffer while
-// the current chunk computes (two buffers).  One thread issues the MMAs; tcgen05.commit
-// arrives on an mbarrier that every thread waits on with an iteration limit (on timeout the
-// CTA records STATUS_TIMEOUT, drains, frees its tensor memory and exits).
+// Warp roles (18 warps):
+//   warp 0      producer: dt, softplus, clamp, in-chunk cumsum and the decay vectors of the
+//               chunk (all lanes), then TMA tile loads of C, B, x into a two-slot stage ring.
+//   warp 1      MMA issuer (one lane) and tensor-memory owner.
+//   warps 2-9   A: the masked, decayed C.B tile M and the scaled B (two warps per TMEM
+//               lane quadrant, one half of the columns each).
+//   warps 10-17 E: state update and y epilogue (two warps per quadrant, each a share of
+//               the 16-column blocks of P).
+// Only the state crosses chunks, so chunk c+1's loads, MMA1 and A work run while E finishes
+// chunk c; C.B^T is double-buffered in tensor memory so MMA1(c+1) runs while A reads chunk c's.
+// Every hand-off is an mbarrier (tcgen05.commit for MMA completion, plain arrives for
+// warps) and every wait is bounded: on timeout the CTA raises an abort flag that all roles
+// poll, records STATUS_TIMEOUT and exits after freeing its tensor memory.
 //
-// Shared-memory operand layouts (bf16, 16-byte chunk = 8 consecutive elements of a row):
-//   C, B tile [128 rows t][128 n]: chunk (r, j) at (r/8)*2048 + j*128 + (r%8)*16.
-//       C is the K-major A operand of MMA1/MMA3 (LBO 128, SBO 2048); B the K-major B operand
-//       of MMA1 and, scaled in place, the MN-major A operand of MMA4 (M = n: SBO 128,
-//       LBO 2048).
-//   X tile [128 rows s][P]: chunk (s, jp) at (s/8)*(16P) + jp*128 + (s%8)*16: the MN-major B
-//       operand (N = p) of MMA2 and MMA4 (SBO 128, LBO 16P).
-//   M tile [128 rows l][128 s]: as C (K-major A operand of MMA2).
-//   Sprev [128 rows n][P]: as X (MN-major B operand of MMA3, K = n).
+// Shared-memory operand layouts (16-byte chunk = 8 bf16 of a row):
+//   C, B tile: two TMA boxes {64 n, 128 t} with 128-byte swizzle, [n half][t][128 B]: K-major
+//       for MMA1 / MMA3 (8-row groups 1024 B, K steps +32 B, second half +16 KB); the scaled B
+//       is also the MN-major A operand of MMA4 (M = n: halves 16 KB apart, K = t groups 1024 B).
+//   X tile: box {64 p, 128 s} with 128-byte swizzle and, for P = 80, box {16 p, 128 s} with
+//       32-byte swizzle: MN-major B operands of MMA2 / MMA4, issued as N = 64 and N = 16 MMAs.
+//   M tile [16 chunks][128 rows l][16 B], no swizzle: K-major A operand of MMA2 (rows 16 B,
+//       8-row groups 128 B, K chunks 2048 B).
+//   Sprev [P/8 chunks][128 rows n][16 B], no swizzle: MN-major B operand of MMA3.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <math.h>
@@ -43,16 +51,18 @@
 namespace nssm {
 namespace scan {
 
-constexpr int kQ = 128;        // tokens per chunk (the MMA M of MMA1/2/3)
-constexpr int kN = 128;        // d_state (the MMA M of MMA4)
-constexpr int kThreads = 256;
+constexpr int kQ = 128;        // tokens per chunk
+constexpr int kN = 128;        // d_state
+constexpr int kWarps = 18;
+constexpr int kThreads = kWarps * 32;
+constexpr int kWA0 = 2, kWE0 = 10;       // first A warp, first E warp
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColCB = 0, kColYoff = 128, kColYdiag = 256, kColSc = 384;
+constexpr uint32_t kColCB0 = 0, kColCB1 = 128, kColYd = 256, kColS = 336, kColYo = 416;
 constexpr int kOp = kQ * kN * 2;   // bytes of a 128 x 128 bf16 tile
 
 struct ScanParams {
   int batch, T, H, G;
-  const __nv_bfloat16* x;
+  const __nv_bfloat16* x;   // read by the epilogue for D x (the MMAs take x through TMA)
   int64_t x_sb, x_st;
   const void* dt;
   int64_t dt_sb, dt_st;
@@ -61,10 +71,6 @@ struct ScanParams {
   const float* A;
   const float* D;
   const float* dt_bias;
-  const __nv_bfloat16* B;
-  int64_t B_sb, B_st;
-  const __nv_bfloat16* C;
-  int64_t C_sb, C_st;
   const float* init;
   int64_t init_sb;
   __nv_bfloat16* y;
@@ -74,18 +80,31 @@ struct ScanParams {
   int32_t* status;
 };
 
+constexpr int kVSlots = 3;                       // chunk vectors ring (dt, cs, fst, eoff, eT)
+constexpr int kVBytes = 4 * kQ * 4 + 32;
+
 template <int P>
 struct Smem {
-  static constexpr int kX = kQ * P * 2;
-  static constexpr int kBuf = 2 * kOp + kX;            // C | B | X of one chunk
-  static constexpr int kM = 2 * kBuf;                  // the masked, decayed C.B tile
-  static constexpr int kSp = kM + kOp;                 // bf16 state entering the chunk
-  static constexpr int kVec = kSp + kN * P * 2;        // dt, cs, fst, eoff [kQ] f32
-  static constexpr int kMisc = kVec + 4 * kQ * 4;      // wtot[4], eT, flag, tmem base, 2 mbarriers
-  static constexpr int kBytes = kMisc + 64;
+  static constexpr int kX = kQ * P * 2;                       // X: 64-column part + (P-64)-column part
+  static constexpr int kStage = 2 * kOp + kX;                 // C | B | X tiles of one chunk
+  static constexpr int kX64 = 2 * kOp, kXt = 2 * kOp + kQ * 64 * 2;   // offsets inside a stage
+  static constexpr int kM = 2 * kStage;
+  static constexpr int kSp = kM + kOp;
+  static constexpr int kVec = kSp + kN * P * 2;
+  static constexpr int kBar = kVec + kVSlots * kVBytes;
+  static constexpr int kBytes = kBar + 256;
+  static constexpr uint32_t kTx = kStage;                     // TMA bytes per stage
+  static_assert(kStage % 1024 == 0, "stage must keep 1 KB alignment");
 };
 
-// ---- tcgen05 / cp.async primitives --------------------------------------------------------
+// mbarrier slots (8 bytes each) at Smem::kBar
+enum : int {
+  B_FULL0 = 0, B_FULL1, B_EMPTY0, B_EMPTY1, B_CBFULL0, B_CBFULL1, B_CBFREE0, B_CBFREE1, B_MFULL, B_MFREE,
+  B_SFULL, B_YFULL, B_SREADY, B_YDFREE, B_SPFULL, B_YOFREE, B_VFULL0, B_VFULL1, B_VFULL2, B_VEMPTY0,
+  B_VEMPTY1, B_VEMPTY2, B_COUNT
+};
+
+// ---- tcgen05 / TMA primitives ------------------------------------------------------------
 // Shared-memory matrix descriptor, no swizzle: start, leading (LBO) and stride (SBO) byte
 // offsets in 16-byte units, version 1 (bits 46-47) for sm_100.
 __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
@@ -111,8 +130,8 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// 16 consecutive fp32 columns of this warp's 32 lanes, waited for inside the same asm so no
-// use of the registers can be scheduled before the data has landed.
+// 16 consecutive fp32 columns of this warp's 32 lanes, waited for inside the same asm so
+// no use of the registers can be scheduled before the data has landed.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   uint32_t r[16];
   asm volatile(
@@ -125,12 +144,29 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
-
-__device__ __forceinline__ void cp16(uint32_t dst, const void* src, uint32_t bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
+// 16 consecutive fp32 columns of this warp's 32 lanes into tensor memory (waited for)
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n"
+      "tcgen05.wait::st.sync.aligned;\n" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+      "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15]))
+      : "memory");
 }
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// 3-D tiled TMA load global -> this CTA's shared memory (no multicast), completing on `bar`
+__device__ __forceinline__ void tma_load3(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
+}
+// descriptor layout types (bits 61-63)
+constexpr uint64_t kSw128 = 2ull << 61, kSw32 = 6ull << 61;
 
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
@@ -140,41 +176,36 @@ __device__ __forceinline__ float2 unpack_bf16(uint32_t w) {
   return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
 }
 
-// Bounded wait for the MMA group committed to `bar` (phase parity `par`); the result is the
-// same on every thread of the CTA.
-__device__ __forceinline__ bool mma_wait(uint64_t* bar, uint32_t par) {
-  const bool ok = mbar_wait_bounded(bar, par);
-  return !__syncthreads_or(!ok);
+// try_wait that lets the thread sleep up to 1 ms for the phase (instead of spinning and taking
+// issue slots from the working warps); true once the phase with `parity` has completed
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
+      : "memory");
+  return ok != 0;
+}
+constexpr uint32_t kWaitTries = 4000;   // at most ~4 s per wait
+
+// Bounded wait that also gives up once another role has raised the abort flag.
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t par, volatile int* abort_flag) {
+  for (uint32_t it = 0;; ++it) {
+    if (mbar_try_wait_sleep(bar, par)) return true;
+    if (*abort_flag) return false;
+    if (it >= kWaitTries) {
+      *abort_flag = 1;
+      return false;
+    }
+  }
 }
 
-// Chunk c of (b, h) into the buffer at shared address `buf`: C, B (group g) and x rows of
-// the chunk's tokens; rows past the sequence end are zero-filled.
-template <int P>
-__device__ __forceinline__ void load_chunk(const ScanParams& p, int b, int h, int g, int c, uint32_t buf, int tid) {
-  const int t0 = c * kQ;
-  const int nvalid = min(kQ, p.T - t0);
-  const __nv_bfloat16* Cb = p.C + (int64_t)b * p.C_sb + (int64_t)g * kN;
-  const __nv_bfloat16* Bb = p.B + (int64_t)b * p.B_sb + (int64_t)g * kN;
-#pragma unroll 4
-  for (int i = tid; i < kQ * kN / 8; i += kThreads) {
-    const int r = ((i >> 7) << 3) | (i & 7), j = (i >> 3) & 15;
-    const bool ok = r < nvalid;
-    const int64_t t = t0 + (ok ? r : 0);
-    cp16(buf + i * 16, Cb + t * p.C_st + j * 8, ok ? 16u : 0u);
-    cp16(buf + kOp + i * 16, Bb + t * p.B_st + j * 8, ok ? 16u : 0u);
-  }
-  const __nv_bfloat16* xb = p.x + (int64_t)b * p.x_sb + (int64_t)h * P;
-  constexpr int kJP = P / 8;
-#pragma unroll 2
-  for (int i = tid; i < kQ * kJP; i += kThreads) {
-    const int grp = i >> 3;
-    const int rhi = grp / kJP, jp = grp - rhi * kJP;
-    const int r = (rhi << 3) | (i & 7);
-    const bool ok = r < nvalid;
-    const int64_t t = t0 + (ok ? r : 0);
-    cp16(buf + 2 * kOp + i * 16, xb + t * p.x_st + jp * 8, ok ? 16u : 0u);
-  }
-  cp_commit();
+// The same wait taken by every lane (each observes the phase, so the data it guards is
+// visible to each), with one outcome for the whole warp so a warp never splits on it.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t par, volatile int* abort_flag) {
+  const bool ok = wait_bar(bar, par, abort_flag);
+  return __all_sync(0xffffffffu, ok);
 }
 
 __device__ __forceinline__ float load_dt(const ScanParams& p, int b, int t, int h) {
@@ -184,288 +215,465 @@ __device__ __forceinline__ float load_dt(const ScanParams& p, int b, int t, int 
 }
 
 template <int P>
-__global__ void __launch_bounds__(kThreads, 1) chunk_scan_kernel(const ScanParams p) {
-  static_assert(P % 16 == 0 && P >= 16 && P <= 128, "headdim must be a multiple of 16 in [16, 128]");
+__global__ void __launch_bounds__(kThreads, 1)
+    chunk_scan_kernel(const ScanParams p, const __grid_constant__ CUtensorMap tmC,
+                      const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmX,
+                      const __grid_constant__ CUtensorMap tmXt) {
+  static_assert(P % 16 == 0 && P >= 32 && P <= 80, "headdim must be a multiple of 16 in [32, 80]");
   using L = Smem<P>;
   extern __shared__ __align__(1024) unsigned char smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int h = blockIdx.x, b = blockIdx.y;
-  const int g = h / (p.H / p.G);
-  const int nch = (p.T + kQ - 1) / kQ;
-
-  float* s_dt = reinterpret_cast<float*>(smem + L::kVec);
-  float* s_cs = s_dt + kQ;
-  float* s_fst = s_cs + kQ;
-  float* s_eoff = s_fst + kQ;
-  float* s_wtot = reinterpret_cast<float*>(smem + L::kMisc);        // [4]
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L::kMisc + 16);
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L::kMisc + 32);  // [2]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L::kBar);
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L::kBar + 8 * B_COUNT);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(smem + L::kBar + 8 * B_COUNT + 4);
   const uint32_t sbase = smem_u32(smem);
-  const uint32_t sM = sbase + L::kM, sSp = sbase + L::kSp;
+
+  const int n_items = p.batch * p.H;
+  const int nch = (p.T + kQ - 1) / kQ;
+  const int my_items = blockIdx.x < n_items ? (n_items - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  const int total = my_items * nch;   // iterations of this CTA's stream
+  const bool have_init = p.init != nullptr;
 
   if (tid == 0) {
-    mbar_init(&bar[0], 1);
-    mbar_init(&bar[1], 1);
+    mbar_init(&bar[B_FULL0], 1);
+    mbar_init(&bar[B_FULL1], 1);
+    mbar_init(&bar[B_EMPTY0], 1);
+    mbar_init(&bar[B_EMPTY1], 1);
+    mbar_init(&bar[B_CBFULL0], 1);
+    mbar_init(&bar[B_CBFULL1], 1);
+    mbar_init(&bar[B_CBFREE0], 8);
+    mbar_init(&bar[B_CBFREE1], 8);
+    mbar_init(&bar[B_MFULL], 8);
+    mbar_init(&bar[B_MFREE], 1);
+    mbar_init(&bar[B_SFULL], 1);
+    mbar_init(&bar[B_YFULL], 1);
+    mbar_init(&bar[B_SREADY], 8);
+    mbar_init(&bar[B_YDFREE], 8);
+    mbar_init(&bar[B_SPFULL], 8);
+    mbar_init(&bar[B_YOFREE], 8);
+    for (int v = 0; v < kVSlots; ++v) {
+      mbar_init(&bar[B_VFULL0 + v], 1);
+      mbar_init(&bar[B_VEMPTY0 + v], 16);   // 8 A warps + 8 E warps
+    }
+    *s_abort = 0;
     fence_mbar_init();
     fence_proxy_async_smem();
   }
-  if (warp == 0) {
+  if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(s_tmem)),
                  "r"(kTmemCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  load_chunk<P>(p, b, h, g, 0, sbase, tid);
+
+  // E role: state rows n = erow (TMEM lane), 16-column blocks [eb0, eb0 + enb) of P (blocks
+  // split between the two warps of a quadrant so every TMEM access is 16-column aligned).  The
+  // running state lives in tensor memory (columns kColS): before chunk c's MMA4 the epilogue
+  // scales it by exp(cs_last) of chunk c (or sets it to that times the initial state at an
+  // item's first chunk), and MMA4 accumulates sum_s Bs[s][n] x[s][p] on top.
+  constexpr int NB = P / 16, NB0 = (NB + 1) / 2, NB1 = NB - NB0;
+  const bool is_e = warp >= kWE0;
+  const int eq = warp & 3, ehalf = (warp - kWE0) >> 2;
+  const int erow = 32 * eq + lane;
+  const int eb0 = ehalf ? NB0 : 0, enb = ehalf ? NB1 : NB0;
+  auto item_bh = [&](int k, int& b, int& h) {
+    const int item = (int)blockIdx.x + k * (int)gridDim.x;
+    b = item / p.H;
+    h = item - b * p.H;
+  };
+  // 16 values of the initial state of this CTA's item k, row erow, columns 16*blk .. +15
+  auto init_block = [&](int k, int blk, float* v) {
+    int b, h;
+    item_bh(k, b, h);
+    const float* src = p.init + (int64_t)b * p.init_sb + ((int64_t)h * P + 16 * blk) * kN + erow;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = src[(int64_t)i * kN];
+  };
+  auto sp_block = [&](int blk, const float* v) {   // bf16 of 16 state columns -> MMA3 operand
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      uint4 w;
+      w.x = pack_bf16(v[8 * hh + 0], v[8 * hh + 1]);
+      w.y = pack_bf16(v[8 * hh + 2], v[8 * hh + 3]);
+      w.z = pack_bf16(v[8 * hh + 4], v[8 * hh + 5]);
+      w.w = pack_bf16(v[8 * hh + 6], v[8 * hh + 7]);
+      *reinterpret_cast<uint4*>(smem + L::kSp + (2 * blk + hh) * 2048 + erow * 16) = w;
+    }
+  };
+  if (is_e && my_items > 0 && have_init) {
+#pragma unroll
+    for (int kb = 0; kb < NB0; ++kb)
+      if (kb < enb) {
+        float v[16];
+        init_block(0, eb0 + kb, v);
+        sp_block(eb0 + kb, v);
+      }
+    fence_proxy_async_smem();
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
 
-  const float A_h = p.A[h];
-  const float D_h = p.D ? p.D[h] : 0.0f;
-  const float bias_h = p.dt_bias ? p.dt_bias[h] : 0.0f;
-
-  // state S[p] of row n = tid - 128 (warps 4-7)
-  float S[P];
-  const bool srow = warp >= 4;
-  const int n_row = tid - 128;
-  const bool have_init = p.init != nullptr;
-  if (srow) {
+  if (warp == 0) {
+    // ------------------------------------------------------------------ producer
+    for (int it = 0; it < total; ++it) {
+      const int s = it & 1, vs = it % kVSlots;
+      const int k = it / nch, c = it - k * nch;
+      int b, h;
+      item_bh(k, b, h);
+      // the chunk's vectors first: they do not wait for the stage
+      if (it >= kVSlots && !warp_wait(&bar[B_VEMPTY0 + vs], (uint32_t)((it / kVSlots - 1) & 1), s_abort)) break;
+      float* v_dt = reinterpret_cast<float*>(smem + L::kVec + vs * kVBytes);
+      float* v_cs = v_dt + kQ;
+      float* v_fst = v_cs + kQ;
+      float* v_eoff = v_fst + kQ;
+      float* v_eT = v_eoff + kQ;
+      const int t0 = c * kQ;
+      const float A_h = p.A[h];
+      const float bias = p.dt_bias ? p.dt_bias[h] : 0.0f;
+      float d[4], cs[4];
+      float run = 0.0f;
 #pragma unroll
-    for (int q = 0; q < P; ++q)
-      S[q] = have_init ? p.init[(int64_t)b * p.init_sb + ((int64_t)h * P + q) * kN + n_row] : 0.0f;
-    if (have_init) {
-#pragma unroll
-      for (int jp = 0; jp < P / 8; ++jp) {
-        uint4 w;
-        w.x = pack_bf16(S[8 * jp + 0], S[8 * jp + 1]);
-        w.y = pack_bf16(S[8 * jp + 2], S[8 * jp + 3]);
-        w.z = pack_bf16(S[8 * jp + 4], S[8 * jp + 5]);
-        w.w = pack_bf16(S[8 * jp + 6], S[8 * jp + 7]);
-        *reinterpret_cast<uint4*>(smem + L::kSp + (n_row >> 3) * (P * 16) + jp * 128 + (n_row & 7) * 16) = w;
+      for (int j = 0; j < 4; ++j) {
+        const int t = t0 + 4 * lane + j;
+        float v = 0.0f;
+        if (t < p.T) {
+          v = load_dt(p, b, t, h) + bias;
+          if (p.softplus) v = softplus_f(v);
+          v = fminf(fmaxf(v, p.dt_lo), p.dt_hi);
+        }
+        d[j] = v;
+        run += v * A_h;
+        cs[j] = run;
       }
-    }
-  }
-
-  float dcur = 0.0f;
-  if (tid < kQ && tid < p.T) dcur = load_dt(p, b, tid, h);
-
-  bool ok = true;
-  uint64_t* fail_bar = &bar[0];
-  uint32_t fail_par = 0;
-  for (int c = 0; c < nch; ++c) {
-    const int cur = c & 1;
-    const uint32_t sC = sbase + cur * L::kBuf, sB = sC + kOp, sX = sC + 2 * kOp;
-    unsigned char* gB = smem + cur * L::kBuf + kOp;
-    const unsigned char* gX = smem + cur * L::kBuf + 2 * kOp;
-    const int t0 = c * kQ;
-    const int nvalid = min(kQ, p.T - t0);
-    const bool have_prev = c > 0 || have_init;
-    const uint32_t par = (uint32_t)(c & 1);
-
-    // ---- dt, dA and the in-chunk inclusive scan of dA (warps 0-3, one token each)
-    float d = 0.0f, cs = 0.0f;
-    if (tid < kQ) {
-      if (tid < nvalid) {
-        d = dcur + bias_h;
-        if (p.softplus) d = softplus_f(d);
-        d = fminf(fmaxf(d, p.dt_lo), p.dt_hi);
-      }
-      cs = d * A_h;
+      float inc = run;   // inclusive scan of the lane totals
 #pragma unroll
       for (int off = 1; off < 32; off <<= 1) {
-        const float u = __shfl_up_sync(0xffffffffu, cs, off);
-        if (lane >= off) cs += u;
+        const float u = __shfl_up_sync(0xffffffffu, inc, off);
+        if (lane >= off) inc += u;
       }
-      if (lane == 31) s_wtot[warp] = cs;
-      const int tn = t0 + kQ + tid;
-      dcur = (tn < p.T) ? load_dt(p, b, tn, h) : 0.0f;
+      const float base = inc - run;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) cs[j] += base;
+      const float last = __shfl_sync(0xffffffffu, cs[3], 31);
+      *reinterpret_cast<float4*>(v_dt + 4 * lane) = make_float4(d[0], d[1], d[2], d[3]);
+      *reinterpret_cast<float4*>(v_cs + 4 * lane) = make_float4(cs[0], cs[1], cs[2], cs[3]);
+      *reinterpret_cast<float4*>(v_fst + 4 * lane) =
+          make_float4(__expf(last - cs[0]) * d[0], __expf(last - cs[1]) * d[1], __expf(last - cs[2]) * d[2],
+                      __expf(last - cs[3]) * d[3]);
+      *reinterpret_cast<float4*>(v_eoff + 4 * lane) =
+          make_float4(__expf(cs[0]), __expf(cs[1]), __expf(cs[2]), __expf(cs[3]));
+      if (lane == 0) *v_eT = __expf(last);
+      __threadfence_block();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar[B_VFULL0 + vs]);
+      // then the tiles, once the stage's previous chunk has left the tensor cores
+      if (it >= 2 && !warp_wait(&bar[B_EMPTY0 + s], (uint32_t)(((it >> 1) - 1) & 1), s_abort)) break;
+      if (lane == 0) {
+        const uint32_t st = sbase + s * L::kStage;
+        const int g = h / (p.H / p.G);
+        mbar_expect_tx(&bar[B_FULL0 + s], L::kTx);
+        tma_load3(st, &tmC, kN * g, t0, b, &bar[B_FULL0 + s]);
+        tma_load3(st + kOp / 2, &tmC, kN * g + 64, t0, b, &bar[B_FULL0 + s]);
+        tma_load3(st + kOp, &tmB, kN * g, t0, b, &bar[B_FULL0 + s]);
+        tma_load3(st + kOp + kOp / 2, &tmB, kN * g + 64, t0, b, &bar[B_FULL0 + s]);
+        tma_load3(st + L::kX64, &tmX, P * h, t0, b, &bar[B_FULL0 + s]);
+        if constexpr (P > 64) tma_load3(st + L::kXt, &tmXt, P * h + 64, t0, b, &bar[B_FULL0 + s]);
+      }
+      __syncwarp();
     }
-    cp_wait_all();
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    // the other buffer was last read by chunk c-1, which is complete
-    if (c + 1 < nch) load_chunk<P>(p, b, h, g, c + 1, sbase + (cur ^ 1) * L::kBuf, tid);
-    if (tid == 0) {
-      tc_fence_after();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
       constexpr uint32_t kIdCB = idesc_bf16(128, 128, 0, 0);
-      constexpr uint32_t kIdYoff = idesc_bf16(128, P, 0, 1);
+      constexpr uint32_t kIdY = idesc_bf16(128, P, 0, 1);
+      constexpr uint32_t kIdY64 = idesc_bf16(128, 64, 0, 1), kIdYt = idesc_bf16(128, P > 64 ? P - 64 : 16, 0, 1);
+      constexpr uint32_t kIdS64 = idesc_bf16(128, 64, 1, 1), kIdSt = idesc_bf16(128, P > 64 ? P - 64 : 16, 1, 1);
+      // x tile: 64 columns with 128-byte swizzle (K groups of 8 rows: 1024 B) and the rest with
+      // 32-byte swizzle (K groups: 256 B); 16 K rows per MMA
+      auto xdesc64 = [&](uint32_t sX, int kk) { return sdesc(sX + L::kX64 + 2048 * kk, 16384, 1024) | kSw128; };
+      auto xdesct = [&](uint32_t sX, int kk) { return sdesc(sX + L::kXt + 512 * kk, 4096, 256) | kSw32; };
+      // C and B: K-major, 128-byte swizzle (8-row groups 1024 B), two 64-column halves 16 KB
+      // apart; K steps of 16 columns are +32 B inside a half
+      auto kdesc = [&](uint32_t base, int kk) {
+        return sdesc(base + (kk >> 2) * (kOp / 2) + (kk & 3) * 32, 16, 1024) | kSw128;
+      };
+      const uint32_t sM = sbase + L::kM, sSp = sbase + L::kSp;
+      // C.B^T of chunk it into CB buffer it & 1 (both tensor-memory CB buffers let chunk it+1's
+      // MMA1 run while the A warps still read chunk it's)
+      auto issue_cb = [&](int it) -> bool {
+        const int s = it & 1;
+        const uint32_t st = sbase + s * L::kStage;
+        if (!wait_bar(&bar[B_FULL0 + s], (uint32_t)((it >> 1) & 1), s_abort)) return false;
+        if (it >= 2 && !wait_bar(&bar[B_CBFREE0 + s], (uint32_t)(((it >> 1) - 1) & 1), s_abort)) return false;
+        tc_fence_after();
+        const uint32_t cb = s ? kColCB1 : kColCB0;
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk)
-        umma(tmem + kColCB, sdesc(sC + 256 * kk, 128, 2048), sdesc(sB + 256 * kk, 128, 2048), kIdCB, kk > 0);
-      if (have_prev) {
+        for (int kk = 0; kk < 8; ++kk) umma(tmem + cb, kdesc(st, kk), kdesc(st + kOp, kk), kIdCB, kk > 0);
+        umma_commit(&bar[B_CBFULL0 + s]);
+        return true;
+      };
+      bool ok = total == 0 || issue_cb(0);
+      for (int it = 0; ok && it < total; ++it) {
+        const int s = it & 1;
+        const int c = it % nch;
+        const uint32_t st = sbase + s * L::kStage, sC = st, sB = st + kOp;
+        const uint32_t pprev = (uint32_t)((it - 1) & 1);
+        if (it + 1 < total && !issue_cb(it + 1)) break;
+        if (c > 0 || have_init) {
+          if (it > 0 && !wait_bar(&bar[B_SPFULL], pprev, s_abort)) break;
+          if (it > 0 && !wait_bar(&bar[B_YOFREE], pprev, s_abort)) break;
+          tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          umma(tmem + kColYoff, sdesc(sC + 256 * kk, 128, 2048), sdesc(sSp + kk * 32 * P, 16 * P, 128), kIdYoff,
-               kk > 0);
+          for (int kk = 0; kk < 8; ++kk)
+            umma(tmem + kColYo, kdesc(sC, kk), sdesc(sSp + 256 * kk, 128, 2048), kIdY, kk > 0);
+        }
+        if (!wait_bar(&bar[B_MFULL], (uint32_t)(it & 1), s_abort)) break;
+        if (!wait_bar(&bar[B_SREADY], (uint32_t)(it & 1), s_abort)) break;
+        tc_fence_after();
+        // S already holds exp(cs_last) * S_prev (the epilogue scaled it): accumulate the chunk.
+        // Scaled B as the MN-major A operand (M = n): 128-byte swizzle, n halves 16 KB apart
+        // (LBO), K groups of 8 token rows 1024 B apart (SBO)
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t a = sdesc(sB + 2048 * kk, 16384, 1024) | kSw128;
+          umma(tmem + kColS, a, xdesc64(st, kk), kIdS64, 1u);
+          if constexpr (P > 64) umma(tmem + kColS + 64, a, xdesct(st, kk), kIdSt, 1u);
+        }
+        umma_commit(&bar[B_SFULL]);
+        if (it > 0 && !wait_bar(&bar[B_YDFREE], pprev, s_abort)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t a = sdesc(sM + 4096 * kk, 2048, 128);
+          umma(tmem + kColYd, a, xdesc64(st, kk), kIdY64, kk > 0);
+          if constexpr (P > 64) umma(tmem + kColYd + 64, a, xdesct(st, kk), kIdYt, kk > 0);
+        }
+        umma_commit(&bar[B_YFULL]);
+        umma_commit(&bar[B_MFREE]);
+        umma_commit(&bar[B_EMPTY0 + s]);
       }
-      umma_commit(&bar[0]);
     }
-    if (tid < kQ) {
-      float base = 0.0f;
-      for (int w = 0; w < warp; ++w) base += s_wtot[w];
-      cs += base;
-      s_dt[tid] = d;
-      s_cs[tid] = cs;
-    }
-    __syncthreads();
-    if (tid < kQ) {
-      const float last = s_cs[kQ - 1];
-      s_fst[tid] = __expf(last - cs) * d;
-      s_eoff[tid] = __expf(cs);
-    }
-    __syncthreads();
-    if (!mma_wait(&bar[0], par)) {
-      ok = false;
-      fail_bar = &bar[0];
-      fail_par = par;
-      break;
-    }
-    tc_fence_after();
-
-    // ---- phase A: M = bf16(mask(CB * exp(cs_l - cs_s) * dt_s)) (rows l = lanes of quadrant
-    // warp%4, columns half warp/4), and B -> bf16(B * exp(cs_last - cs_s) * dt_s) in place.
-    {
-      const int rq = warp & 3, half = warp >> 2;
-      const int l = 32 * rq + lane;
-      const float cs_l = s_cs[l];
+    __syncwarp();
+  } else if (!is_e) {
+    // ------------------------------------------------------------------ A: M tile, scaled B
+    const int q = warp & 3, half = (warp - kWA0) >> 2;
+    const int l = 32 * q + lane;
+    const int a_idx = (warp - kWA0) * 32 + lane;   // 0..255
+    for (int it = 0; it < total; ++it) {
+      const int s = it & 1, vs = it % kVSlots;
+      unsigned char* stg = smem + s * L::kStage;
+      const float* v_dt = reinterpret_cast<const float*>(smem + L::kVec + vs * kVBytes);
+      const float* v_cs = v_dt + kQ;
+      const float* v_fst = v_cs + kQ;
+      if (!warp_wait(&bar[B_VFULL0 + vs], (uint32_t)((it / kVSlots) & 1), s_abort)) break;
+      if (!warp_wait(&bar[B_FULL0 + s], (uint32_t)((it >> 1) & 1), s_abort)) break;
+      if (!warp_wait(&bar[B_CBFULL0 + s], (uint32_t)((it >> 1) & 1), s_abort)) break;
+      if (it > 0 && !warp_wait(&bar[B_MFREE], (uint32_t)((it - 1) & 1), s_abort)) break;
+      tc_fence_after();
+      const float cs_l = v_cs[l];
+      const uint32_t cb = (s ? kColCB1 : kColCB0) + ((uint32_t)(32 * q) << 16);
 #pragma unroll
       for (int blk = 0; blk < 4; ++blk) {
         const int s0 = 64 * half + 16 * blk;
         uint4 w0 = make_uint4(0, 0, 0, 0), w1 = make_uint4(0, 0, 0, 0);
-        if (s0 <= 32 * rq + 31) {   // some s <= l in this block (warp-uniform)
+        if (s0 <= 32 * q + 31) {   // some s <= l in this block (warp-uniform)
           float v[16];
-          tmem_ld16(tmem + ((uint32_t)(32 * rq) << 16) + kColCB + s0, v);
+          tmem_ld16(tmem + cb + s0, v);
           float m[16];
 #pragma unroll
-          for (int k = 0; k < 16; ++k) {
-            const int s = s0 + k;
-            m[k] = (s <= l) ? (v[k] * __expf(cs_l - s_cs[s])) * s_dt[s] : 0.0f;
+          for (int k4 = 0; k4 < 4; ++k4) {
+            const float4 c4 = *reinterpret_cast<const float4*>(v_cs + s0 + 4 * k4);
+            const float4 d4 = *reinterpret_cast<const float4*>(v_dt + s0 + 4 * k4);
+            const float cv[4] = {c4.x, c4.y, c4.z, c4.w}, dv[4] = {d4.x, d4.y, d4.z, d4.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int kx = 4 * k4 + j;
+              m[kx] = (s0 + kx <= l) ? (v[kx] * __expf(cs_l - cv[j])) * dv[j] : 0.0f;
+            }
           }
           w0 = make_uint4(pack_bf16(m[0], m[1]), pack_bf16(m[2], m[3]), pack_bf16(m[4], m[5]), pack_bf16(m[6], m[7]));
           w1 = make_uint4(pack_bf16(m[8], m[9]), pack_bf16(m[10], m[11]), pack_bf16(m[12], m[13]),
                           pack_bf16(m[14], m[15]));
         }
-        unsigned char* row = smem + L::kM + (l >> 3) * 2048 + (s0 >> 3) * 128 + (l & 7) * 16;
-        *reinterpret_cast<uint4*>(row) = w0;
-        *reinterpret_cast<uint4*>(row + 128) = w1;
+        unsigned char* mrow = smem + L::kM + (s0 >> 3) * 2048 + l * 16;
+        *reinterpret_cast<uint4*>(mrow) = w0;
+        *reinterpret_cast<uint4*>(mrow + 2048) = w1;
       }
-#pragma unroll 2
-      for (int i = tid; i < kQ * kN / 8; i += kThreads) {
-        const int s = ((i >> 7) << 3) | (i & 7);
-        const float f = s_fst[s];
-        uint4* q = reinterpret_cast<uint4*>(gB + i * 16);
-        uint4 w = *q;
-        float2 a0 = unpack_bf16(w.x), a1 = unpack_bf16(w.y), a2 = unpack_bf16(w.z), a3 = unpack_bf16(w.w);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar[B_CBFREE0 + s]);
+      unsigned char* bt = stg + kOp;
+#pragma unroll
+      for (int k2 = 0; k2 < 8; ++k2) {
+        // 16-byte chunk i of the swizzled tile holds 8 n of token row (i / 8) % 128
+        const int i = a_idx + 256 * k2;
+        const float f = v_fst[(i >> 3) & 127];
+        uint4* qp = reinterpret_cast<uint4*>(bt + i * 16);
+        uint4 w = *qp;
+        const float2 a0 = unpack_bf16(w.x), a1 = unpack_bf16(w.y), a2 = unpack_bf16(w.z), a3 = unpack_bf16(w.w);
         w.x = pack_bf16(a0.x * f, a0.y * f);
         w.y = pack_bf16(a1.x * f, a1.y * f);
         w.z = pack_bf16(a2.x * f, a2.y * f);
         w.w = pack_bf16(a3.x * f, a3.y * f);
-        *q = w;
+        *qp = w;
       }
-    }
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
-      tc_fence_after();
-      constexpr uint32_t kIdY = idesc_bf16(128, P, 0, 1);
-      constexpr uint32_t kIdS = idesc_bf16(128, P, 1, 1);
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk)
-        umma(tmem + kColYdiag, sdesc(sM + 256 * kk, 128, 2048), sdesc(sX + kk * 32 * P, 16 * P, 128), kIdY, kk > 0);
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk)
-        umma(tmem + kColSc, sdesc(sB + 4096 * kk, 2048, 128), sdesc(sX + kk * 32 * P, 16 * P, 128), kIdS, kk > 0);
-      umma_commit(&bar[1]);
-    }
-    if (!mma_wait(&bar[1], par)) {
-      ok = false;
-      fail_bar = &bar[1];
-      fail_par = par;
-      break;
-    }
-    tc_fence_after();
-
-    // ---- phase B
-    if (!srow) {
-      // y rows l = tid (warps 0-3): y = Yoff * exp(cs_l) + Ydiag + D x
-      const int l = tid;
-      const float el = s_eoff[l];
-      const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
-      __nv_bfloat16* yrow = p.y + (int64_t)b * p.y_sb + (int64_t)(t0 + (l < nvalid ? l : 0)) * p.y_st + (int64_t)h * P;
-      const unsigned char* xrow = gX + (l >> 3) * (P * 16) + (l & 7) * 16;
-#pragma unroll
-      for (int jb = 0; jb < P / 16; ++jb) {
-        float yo[16], yd[16];
-        tmem_ld16(tmem + lane_base + kColYdiag + 16 * jb, yd);
-        if (have_prev) {
-          tmem_ld16(tmem + lane_base + kColYoff + 16 * jb, yo);
-        } else {
-#pragma unroll
-          for (int k = 0; k < 16; ++k) yo[k] = 0.0f;
-        }
-        const uint4 xa = *reinterpret_cast<const uint4*>(xrow + (2 * jb) * 128);
-        const uint4 xb = *reinterpret_cast<const uint4*>(xrow + (2 * jb + 1) * 128);
-        const uint32_t xw[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-        uint32_t o[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const float2 xv = unpack_bf16(xw[k]);
-          const float v0 = (yo[2 * k] * el + yd[2 * k]) + xv.x * D_h;
-          const float v1 = (yo[2 * k + 1] * el + yd[2 * k + 1]) + xv.y * D_h;
-          o[k] = pack_bf16(v0, v1);
-        }
-        if (l < nvalid) {
-          uint4* dst = reinterpret_cast<uint4*>(yrow + 16 * jb);
-          dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
-          dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
-        }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&bar[B_MFULL]);
+        mbar_arrive(&bar[B_VEMPTY0 + vs]);
       }
-    } else {
-      // state rows n (warps 4-7): S = exp(cs_last) S + Sc, then the bf16 copy for the next chunk
-      const float eT = __expf(s_cs[kQ - 1]);
-      const uint32_t lane_base = (uint32_t)(32 * (warp - 4)) << 16;
-#pragma unroll
-      for (int jb = 0; jb < P / 16; ++jb) {
-        float sc[16];
-        tmem_ld16(tmem + lane_base + kColSc + 16 * jb, sc);
-#pragma unroll
-        for (int k = 0; k < 16; ++k) S[16 * jb + k] = fmaf(eT, S[16 * jb + k], sc[k]);
-      }
-      if (c + 1 < nch) {
-#pragma unroll
-        for (int jp = 0; jp < P / 8; ++jp) {
-          uint4 w;
-          w.x = pack_bf16(S[8 * jp + 0], S[8 * jp + 1]);
-          w.y = pack_bf16(S[8 * jp + 2], S[8 * jp + 3]);
-          w.z = pack_bf16(S[8 * jp + 4], S[8 * jp + 5]);
-          w.w = pack_bf16(S[8 * jp + 6], S[8 * jp + 7]);
-          *reinterpret_cast<uint4*>(smem + L::kSp + (n_row >> 3) * (P * 16) + jp * 128 + (n_row & 7) * 16) = w;
-        }
-      }
-    }
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-  }
-
-  if (ok) {
-    if (srow && p.fin) {
-      float* f = p.fin + (int64_t)b * p.fin_sb + (int64_t)h * P * kN + n_row;
-#pragma unroll
-      for (int q = 0; q < P; ++q) f[(int64_t)q * kN] = S[q];
     }
   } else {
-    if (tid == 0 && p.status) atomicOr(p.status, STATUS_TIMEOUT);
-    // give the MMA group that did not complete a last bounded chance before the memory goes
-    mbar_wait_bounded(fail_bar, fail_par);
+    // ------------------------------------------------------------------ E: state, y
+    const uint32_t lane_base = (uint32_t)(32 * eq) << 16;
+    // S <- scale * (S or the initial state of item k): the state MMA4 of the next chunk adds to
+    if (total > 0 && warp_wait(&bar[B_VFULL0], 0u, s_abort)) {   // the state chunk 0's MMA4 adds to
+      const float eT0 = *(reinterpret_cast<const float*>(smem + L::kVec) + 4 * kQ);
+#pragma unroll
+      for (int kb = 0; kb < NB0; ++kb)
+        if (kb < enb) {
+          float v[16];
+          if (have_init) {
+            init_block(0, eb0 + kb, v);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = 0.0f;
+          }
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[i] *= eT0;
+          tmem_st16(tmem + lane_base + kColS + 16 * (eb0 + kb), v);
+        }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar[B_SREADY]);
+    }
+    for (int it = 0; it < total; ++it) {
+      const int s = it & 1, vs = it % kVSlots;
+      const int k = it / nch, c = it - k * nch;
+      const bool last = c == nch - 1;
+      int b, h;
+      item_bh(k, b, h);
+      const float* v_eoff = reinterpret_cast<const float*>(smem + L::kVec + vs * kVBytes) + 3 * kQ;
+      // x of this thread's token row and column blocks, for D x (global, L2-resident: the
+      // chunk's TMA load brought it in), fetched before the waits to hide its latency
+      const int t = c * kQ + erow;
+      const __nv_bfloat16* xrow =
+          p.x + (int64_t)b * p.x_sb + (int64_t)(t < p.T ? t : 0) * p.x_st + (int64_t)h * P;
+      uint4 xr[2 * NB0];
+#pragma unroll
+      for (int kb = 0; kb < NB0; ++kb)
+        if (kb < enb) {
+          xr[2 * kb] = __ldg(reinterpret_cast<const uint4*>(xrow + 16 * (eb0 + kb)));
+          xr[2 * kb + 1] = __ldg(reinterpret_cast<const uint4*>(xrow + 16 * (eb0 + kb) + 8));
+        }
+      if (!warp_wait(&bar[B_VFULL0 + vs], (uint32_t)((it / kVSlots) & 1), s_abort)) break;
+      if (!warp_wait(&bar[B_SFULL], (uint32_t)(it & 1), s_abort)) break;
+      tc_fence_after();
+      // S after chunk c: the bf16 copy for MMA3 of chunk c+1 (or the final state), then S
+      // scaled for chunk it+1's MMA4 (at an item's last chunk: the next item's initial state)
+      const bool more = it + 1 < total;
+      float eT1 = 0.0f;
+      if (more) {
+        const int vs1 = (it + 1) % kVSlots;
+        if (!warp_wait(&bar[B_VFULL0 + vs1], (uint32_t)(((it + 1) / kVSlots) & 1), s_abort)) break;
+        eT1 = *(reinterpret_cast<const float*>(smem + L::kVec + vs1 * kVBytes) + 4 * kQ);
+      }
+      float* fin = p.fin ? p.fin + (int64_t)b * p.fin_sb + (int64_t)h * P * kN + erow : nullptr;
+#pragma unroll
+      for (int kb = 0; kb < NB0; ++kb) {
+        if (kb < enb) {
+          const int blk = eb0 + kb;
+          float cur[16];
+          tmem_ld16(tmem + lane_base + kColS + 16 * blk, cur);
+          if (last) {
+            if (fin) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) fin[(int64_t)(16 * blk + i) * kN] = cur[i];
+            }
+            if (more) {
+              if (have_init) {
+                init_block(k + 1, blk, cur);
+                sp_block(blk, cur);
+              } else {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) cur[i] = 0.0f;
+              }
+            }
+          } else {
+            sp_block(blk, cur);
+          }
+          if (more) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) cur[i] *= eT1;
+            tmem_st16(tmem + lane_base + kColS + 16 * blk, cur);
+          }
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&bar[B_SPFULL]);
+        if (more) mbar_arrive(&bar[B_SREADY]);
+      }
+
+      if (!warp_wait(&bar[B_YFULL], (uint32_t)(it & 1), s_abort)) break;
+      tc_fence_after();
+      const float el = v_eoff[erow];
+      const float D_h = p.D ? p.D[h] : 0.0f;
+      const bool prev = c > 0 || have_init;
+      const uint32_t yo = kColYo;
+      __nv_bfloat16* yrow = p.y + (int64_t)b * p.y_sb + (int64_t)(t < p.T ? t : 0) * p.y_st + (int64_t)h * P;
+#pragma unroll
+      for (int kb = 0; kb < NB0; ++kb) {
+        if (kb < enb) {
+          const int col = 16 * (eb0 + kb);
+          float yd[16], yv[16];
+          tmem_ld16(tmem + lane_base + kColYd + col, yd);
+          if (prev) {
+            tmem_ld16(tmem + lane_base + yo + col, yv);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) yv[i] = 0.0f;
+          }
+          uint32_t o[8];
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            const uint4 xw = xr[2 * kb + hh];
+            const uint32_t xs[4] = {xw.x, xw.y, xw.z, xw.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float2 xv = unpack_bf16(xs[i]);
+              const int j = 8 * hh + 2 * i;
+              const float v0 = (yv[j] * el + yd[j]) + xv.x * D_h;
+              const float v1 = (yv[j + 1] * el + yd[j + 1]) + xv.y * D_h;
+              o[4 * hh + i] = pack_bf16(v0, v1);
+            }
+          }
+          if (t < p.T) {
+            uint4* dst = reinterpret_cast<uint4*>(yrow + col);
+            dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+            dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&bar[B_YDFREE]);
+        mbar_arrive(&bar[B_YOFREE]);
+        mbar_arrive(&bar[B_VEMPTY0 + vs]);
+      }
+    }
   }
-  cp_wait_all();
+
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (tid == 0 && *s_abort && p.status) atomicOr(p.status, STATUS_TIMEOUT);
+  if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
   }

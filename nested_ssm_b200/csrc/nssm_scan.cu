@@ -56,7 +56,7 @@ int encode_tiles(PFN_cuTensorMapEncodeTiled_v12000 enc, CUtensorMap* m, const vo
 
 template <int P>
 int launch(const nssm::scan::ScanParams& sp, const CUtensorMap& mC, const CUtensorMap& mB, const CUtensorMap& mX,
-           const CUtensorMap& mXt, cudaStream_t st) {
+           cudaStream_t st) {
   using L = nssm::scan::Smem<P>;
   static_assert(L::kBytes <= 232448, "shared memory beyond the per-CTA limit");
   cudaError_t e = cudaFuncSetAttribute(nssm::scan::chunk_scan_kernel<P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -72,7 +72,7 @@ int launch(const nssm::scan::ScanParams& sp, const CUtensorMap& mC, const CUtens
   }
   const int items = sp.batch * sp.H;
   const int grid = items < sms ? items : sms;   // one persistent CTA per SM (226 KB shared memory each)
-  nssm::scan::chunk_scan_kernel<P><<<grid, nssm::scan::kThreads, L::kBytes, st>>>(sp, mC, mB, mX, mXt);
+  nssm::scan::chunk_scan_kernel<P><<<grid, nssm::scan::kThreads, L::kBytes, st>>>(sp, mC, mB, mX);
   e = cudaGetLastError();
   if (e != cudaSuccess) return fail(NSSM_ERR_CUDA, "chunk_scan_kernel launch: %s", cudaGetErrorString(e));
   return NSSM_OK;
@@ -112,18 +112,16 @@ int nssm_chunk_scan(const nssm_scan_args* a, void* stream) {
   PFN_cuTensorMapEncodeTiled_v12000 enc = nullptr;
   int rc = get_encode(&enc);
   if (rc) return rc;
-  // C, B: two 64-column boxes per 128-column group tile; x: a 64-column box (128-byte
-  // swizzle) and, for headdim 80, a 16-column box (32-byte swizzle)
-  alignas(64) CUtensorMap mC, mB, mX, mXt;
+  // C, B: two 64-column boxes (128-byte swizzle) per 128-column group tile; x: 16-column boxes
+  // (32-byte swizzle)
+  alignas(64) CUtensorMap mC, mB, mX;
   const int gw = a->ngroups * a->dstate, xw = a->nheads * a->headdim;
   if ((rc = encode_tiles(enc, &mC, a->C, gw, a->seqlen, a->batch, a->C_stride_t, a->C_stride_b, 64,
                          CU_TENSOR_MAP_SWIZZLE_128B, "C")) ||
       (rc = encode_tiles(enc, &mB, a->B, gw, a->seqlen, a->batch, a->B_stride_t, a->B_stride_b, 64,
                          CU_TENSOR_MAP_SWIZZLE_128B, "B")) ||
-      (rc = encode_tiles(enc, &mX, a->x, xw, a->seqlen, a->batch, a->x_stride_t, a->x_stride_b, 64,
-                         CU_TENSOR_MAP_SWIZZLE_128B, "x")) ||
-      (rc = encode_tiles(enc, &mXt, a->x, xw, a->seqlen, a->batch, a->x_stride_t, a->x_stride_b, 16,
-                         CU_TENSOR_MAP_SWIZZLE_32B, "x tail")))
+      (rc = encode_tiles(enc, &mX, a->x, xw, a->seqlen, a->batch, a->x_stride_t, a->x_stride_b, 16,
+                         CU_TENSOR_MAP_SWIZZLE_32B, "x")))
     return rc;
   nssm::scan::ScanParams sp{};
   sp.batch = a->batch; sp.T = a->seqlen; sp.H = a->nheads; sp.G = a->ngroups;
@@ -136,7 +134,7 @@ int nssm_chunk_scan(const nssm_scan_args* a, void* stream) {
   sp.fin = a->final_states; sp.fin_sb = a->final_stride_b;
   sp.status = a->status;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  return a->headdim == 64 ? launch<64>(sp, mC, mB, mX, mXt, st) : launch<80>(sp, mC, mB, mX, mXt, st);
+  return a->headdim == 64 ? launch<64>(sp, mC, mB, mX, st) : launch<80>(sp, mC, mB, mX, st);
 }
 
 }  // extern "C"

@@ -33,8 +33,8 @@
 //   C, B tile: two TMA boxes {64 n, 128 t} with 128-byte swizzle, [n half][t][128 B]: K-major
 //       for MMA1 / MMA3 (8-row groups 1024 B, K steps +32 B, second half +16 KB); the scaled B
 //       is also the MN-major A operand of MMA4 (M = n: halves 16 KB apart, K = t groups 1024 B).
-//   X tile: box {64 p, 128 s} with 128-byte swizzle and, for P = 80, box {16 p, 128 s} with
-//       32-byte swizzle: MN-major B operands of MMA2 / MMA4, issued as N = 64 and N = 16 MMAs.
+//   X tile: P/16 boxes {16 p, 128 s} with 32-byte swizzle, [p group][s][32 B]: MN-major B
+//       operand of MMA2 / MMA4 (16-column groups 4 KB apart, K groups of 8 rows 256 B).
 //   M tile [16 chunks][128 rows l][16 B], no swizzle: K-major A operand of MMA2 (rows 16 B,
 //       8-row groups 128 B, K chunks 2048 B).
 //   Sprev [P/8 chunks][128 rows n][16 B], no swizzle: MN-major B operand of MMA3.
@@ -85,9 +85,8 @@ constexpr int kVBytes = 4 * kQ * 4 + 32;
 
 template <int P>
 struct Smem {
-  static constexpr int kX = kQ * P * 2;                       // X: 64-column part + (P-64)-column part
+  static constexpr int kX = kQ * P * 2;                       // X: P/16 tiles of [128 s][16 p]
   static constexpr int kStage = 2 * kOp + kX;                 // C | B | X tiles of one chunk
-  static constexpr int kX64 = 2 * kOp, kXt = 2 * kOp + kQ * 64 * 2;   // offsets inside a stage
   static constexpr int kM = 2 * kStage;
   static constexpr int kSp = kM + kOp;
   static constexpr int kVec = kSp + kN * P * 2;
@@ -208,6 +207,14 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t par, volatile 
   return __all_sync(0xffffffffu, ok);
 }
 
+// 2^x, flushing subnormal results to zero (one MUFU op)
+__device__ __forceinline__ float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+constexpr float kLog2e = 1.4426950408889634f;
+
 __device__ __forceinline__ float load_dt(const ScanParams& p, int b, int t, int h) {
   const int64_t i = (int64_t)b * p.dt_sb + (int64_t)t * p.dt_st + h;
   return p.dt_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.dt)[i])
@@ -217,8 +224,7 @@ __device__ __forceinline__ float load_dt(const ScanParams& p, int b, int t, int 
 template <int P>
 __global__ void __launch_bounds__(kThreads, 1)
     chunk_scan_kernel(const ScanParams p, const __grid_constant__ CUtensorMap tmC,
-                      const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmX,
-                      const __grid_constant__ CUtensorMap tmXt) {
+                      const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmX) {
   static_assert(P % 16 == 0 && P >= 32 && P <= 80, "headdim must be a multiple of 16 in [32, 80]");
   using L = Smem<P>;
   extern __shared__ __align__(1024) unsigned char smem[];
@@ -356,15 +362,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float base = inc - run;
 #pragma unroll
       for (int j = 0; j < 4; ++j) cs[j] += base;
+      // exponentials in base 2 of log2(e)-scaled cumsums (v_cs holds cs * log2 e)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) cs[j] *= kLog2e;
       const float last = __shfl_sync(0xffffffffu, cs[3], 31);
       *reinterpret_cast<float4*>(v_dt + 4 * lane) = make_float4(d[0], d[1], d[2], d[3]);
       *reinterpret_cast<float4*>(v_cs + 4 * lane) = make_float4(cs[0], cs[1], cs[2], cs[3]);
       *reinterpret_cast<float4*>(v_fst + 4 * lane) =
-          make_float4(__expf(last - cs[0]) * d[0], __expf(last - cs[1]) * d[1], __expf(last - cs[2]) * d[2],
-                      __expf(last - cs[3]) * d[3]);
+          make_float4(ex2_ftz(last - cs[0]) * d[0], ex2_ftz(last - cs[1]) * d[1], ex2_ftz(last - cs[2]) * d[2],
+                      ex2_ftz(last - cs[3]) * d[3]);
       *reinterpret_cast<float4*>(v_eoff + 4 * lane) =
-          make_float4(__expf(cs[0]), __expf(cs[1]), __expf(cs[2]), __expf(cs[3]));
-      if (lane == 0) *v_eT = __expf(last);
+          make_float4(ex2_ftz(cs[0]), ex2_ftz(cs[1]), ex2_ftz(cs[2]), ex2_ftz(cs[3]));
+      if (lane == 0) *v_eT = ex2_ftz(last);
       __threadfence_block();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[B_VFULL0 + vs]);
@@ -378,8 +387,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load3(st + kOp / 2, &tmC, kN * g + 64, t0, b, &bar[B_FULL0 + s]);
         tma_load3(st + kOp, &tmB, kN * g, t0, b, &bar[B_FULL0 + s]);
         tma_load3(st + kOp + kOp / 2, &tmB, kN * g + 64, t0, b, &bar[B_FULL0 + s]);
-        tma_load3(st + L::kX64, &tmX, P * h, t0, b, &bar[B_FULL0 + s]);
-        if constexpr (P > 64) tma_load3(st + L::kXt, &tmXt, P * h + 64, t0, b, &bar[B_FULL0 + s]);
+#pragma unroll
+        for (int j = 0; j < P / 16; ++j) tma_load3(st + 2 * kOp + 4096 * j, &tmX, P * h + 16 * j, t0, b, &bar[B_FULL0 + s]);
       }
       __syncwarp();
     }
@@ -388,12 +397,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t kIdCB = idesc_bf16(128, 128, 0, 0);
       constexpr uint32_t kIdY = idesc_bf16(128, P, 0, 1);
-      constexpr uint32_t kIdY64 = idesc_bf16(128, 64, 0, 1), kIdYt = idesc_bf16(128, P > 64 ? P - 64 : 16, 0, 1);
-      constexpr uint32_t kIdS64 = idesc_bf16(128, 64, 1, 1), kIdSt = idesc_bf16(128, P > 64 ? P - 64 : 16, 1, 1);
-      // x tile: 64 columns with 128-byte swizzle (K groups of 8 rows: 1024 B) and the rest with
-      // 32-byte swizzle (K groups: 256 B); 16 K rows per MMA
-      auto xdesc64 = [&](uint32_t sX, int kk) { return sdesc(sX + L::kX64 + 2048 * kk, 16384, 1024) | kSw128; };
-      auto xdesct = [&](uint32_t sX, int kk) { return sdesc(sX + L::kXt + 512 * kk, 4096, 256) | kSw32; };
+      constexpr uint32_t kIdS = idesc_bf16(128, P, 1, 1);
+      // x tile: MN-major with 32-byte swizzle, 16-column groups 4096 B apart (LBO), K groups of
+      // 8 token rows 256 B apart (SBO); 16 K rows per MMA
+      auto xdesc = [&](uint32_t st, int kk) { return sdesc(st + 2 * kOp + 512 * kk, 4096, 256) | kSw32; };
       // C and B: K-major, 128-byte swizzle (8-row groups 1024 B), two 64-column halves 16 KB
       // apart; K steps of 16 columns are +32 B inside a half
       auto kdesc = [&](uint32_t base, int kk) {
@@ -436,20 +443,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Scaled B as the MN-major A operand (M = n): 128-byte swizzle, n halves 16 KB apart
         // (LBO), K groups of 8 token rows 1024 B apart (SBO)
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t a = sdesc(sB + 2048 * kk, 16384, 1024) | kSw128;
-          umma(tmem + kColS, a, xdesc64(st, kk), kIdS64, 1u);
-          if constexpr (P > 64) umma(tmem + kColS + 64, a, xdesct(st, kk), kIdSt, 1u);
-        }
+        for (int kk = 0; kk < 8; ++kk)
+          umma(tmem + kColS, sdesc(sB + 2048 * kk, 16384, 1024) | kSw128, xdesc(st, kk), kIdS, 1u);
         umma_commit(&bar[B_SFULL]);
         if (it > 0 && !wait_bar(&bar[B_YDFREE], pprev, s_abort)) break;
         tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t a = sdesc(sM + 4096 * kk, 2048, 128);
-          umma(tmem + kColYd, a, xdesc64(st, kk), kIdY64, kk > 0);
-          if constexpr (P > 64) umma(tmem + kColYd + 64, a, xdesct(st, kk), kIdYt, kk > 0);
-        }
+        for (int kk = 0; kk < 8; ++kk) umma(tmem + kColYd, sdesc(sM + 4096 * kk, 2048, 128), xdesc(st, kk), kIdY, kk > 0);
         umma_commit(&bar[B_YFULL]);
         umma_commit(&bar[B_MFREE]);
         umma_commit(&bar[B_EMPTY0 + s]);
@@ -490,7 +490,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               const int kx = 4 * k4 + j;
-              m[kx] = (s0 + kx <= l) ? (v[kx] * __expf(cs_l - cv[j])) * dv[j] : 0.0f;
+              m[kx] = (s0 + kx <= l) ? (v[kx] * ex2_ftz(cs_l - cv[j])) * dv[j] : 0.0f;
             }
           }
           w0 = make_uint4(pack_bf16(m[0], m[1]), pack_bf16(m[2], m[3]), pack_bf16(m[4], m[5]), pack_bf16(m[6], m[7]));

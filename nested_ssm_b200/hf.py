@@ -1,13 +1,17 @@
 """Drop-in for the reference's HF integration: ``install(model, pb, c, ...)`` puts the tiered
 decode state op into a transformers NemotronH model's Mamba2 mixers.
 
-Mirrors ``install`` / ``_dispatch`` / ``_v4_decode`` of scale/v4_native_decode.py:26-256:
-prefill (or any call that is not a one-token decode with a cache) runs the model's own
-torch forward, after which the final recurrent state of every row is split into a tiered
-slot pool; each one-token decode then runs in_proj, ``conv_step`` (conv1d update of the HF
-cache's conv state, SiLU, split, rotation by the mixer's ``ActRotMask`` R when it has one),
-``tiered_state_update``, ``gated_rmsnorm`` (the mixer's norm) and out_proj.  The decode path runs
-on the GPU only; the model's weights and cache must live on a CUDA device.
+Mirrors ``install`` / ``_dispatch`` / ``_lean_prefill`` / ``_v4_decode`` of
+scale/v4_native_decode.py:26-256.  Prefill with a cache runs the lean prefill when
+``lean_prefill`` (the reference's default) and the shapes are compiled (bf16, headdim 64 / 80,
+d_state 128, chunk 128): in_proj, the model's conv1d + SiLU over the prompt, the rotation of B
+and C by the mixer's ``ActRotMask`` R (``rot_flat``), ``mamba_chunk_scan_combined`` (the
+tcgen05 chunk scan) with the final states into the cache, ``gated_rmsnorm``, out_proj; other
+prefills run the model's own torch forward (the reference's ``lean_prefill=0``).  Either way
+the final recurrent state of every row is then split into a tiered slot pool, and each
+one-token decode runs in_proj, ``conv_step`` (conv1d update of the HF cache's conv state,
+SiLU, split, rotation), ``tiered_state_update``, ``gated_rmsnorm`` and out_proj.  The model's
+weights and cache must live on a CUDA device.
 
 Cold storage: ``cold="fp32"`` reproduces the reference's ``cold_bf16=0`` to fp32 rounding;
 ``"bf16"`` / ``"fp8"`` keep the cold slice only in that dtype (dequantise, replay,
@@ -15,9 +19,12 @@ requantise every c tokens), where the reference re-snapshots a full fp32 state.
 """
 from __future__ import annotations
 
-import torch
+import math
 
-from .ops import conv_step, gated_rmsnorm, prefill_split, tiered_state_update
+import torch
+import torch.nn.functional as F
+
+from .ops import conv_step, gated_rmsnorm, mamba_chunk_scan_combined, prefill_split, rot_flat, tiered_state_update
 from .pool import TieredSlotPool
 
 _MODES = {(0, 0): "stale", (1, 0): "corr", (0, 1): "coldoff"}
@@ -60,12 +67,63 @@ def _decode(self, input_states, cache_params):
     y = torch.empty(b, H, P, dtype=dtype, device=input_states.device)
     tiered_state_update(st["pool"], 0, x, dt[:, 0], A, Bv, Cv, self.D, self.dt_bias, True, st["slots"], -1, y,
                         None, self.time_step_min, st["mode"])
+    scan_output = _norm(self, y.reshape(b, 1, I), gate)
+    return self.out_proj(scan_output.to(dtype))
+
+
+def _norm(self, y, gate):
     norm = self.norm
     if all(hasattr(norm, a) for a in ("weight", "variance_epsilon", "group_size")):   # Zamba2RMSNormGated
-        scan_output = gated_rmsnorm(y.reshape(b, 1, I), gate, norm.weight, norm.variance_epsilon, norm.group_size)
-    else:
-        scan_output = norm(y.reshape(b, 1, I), gate)
-    return self.out_proj(scan_output.to(dtype))
+        return gated_rmsnorm(y, gate, norm.weight, norm.variance_epsilon, norm.group_size)
+    return norm(y, gate)
+
+
+def _lean_ok(self, input_states) -> bool:
+    """Shapes the chunk scan is compiled for (else the model's own prefill runs)."""
+    return (input_states.is_cuda and input_states.dtype == torch.bfloat16 and self.head_dim in (64, 80)
+            and self.ssm_state_size == 128 and getattr(self, "chunk_size", 0) == 128 and _is_silu_like(self))
+
+
+def _is_silu_like(self) -> bool:
+    act = self.act.act if (hasattr(self.act, "R") and hasattr(self.act, "act")) else self.act
+    return _is_silu(act)
+
+
+def _lean_prefill(self, input_states, cache_params, attention_mask):
+    """The memory-lean prefill (scale/v4_native_decode.py:175-220) on the GPU kernels: conv1d +
+    SiLU over the prompt (the model's own conv, activation in fp32), B and C rotated by R,
+    the chunk scan with its final states into the cache, the gated norm, out_proj."""
+    st = self._nssm
+    b, T, _ = input_states.shape
+    dtype = input_states.dtype
+    if attention_mask is not None and not torch.all(attention_mask == 1):
+        input_states = (input_states * attention_mask[:, :, None]).to(dtype)
+    H, P, N, G = self.num_heads, self.head_dim, self.ssm_state_size, self.n_groups
+    I, GN = self.intermediate_size, G * N
+    proj = self.in_proj(input_states)
+    d_mlp = (proj.shape[-1] - 2 * I - 2 * GN - H) // 2
+    _, _, gate, xbc, dt = proj.split([d_mlp, d_mlp, I, self.conv_dim, H], dim=-1)
+    xbc_t = xbc.transpose(1, 2)
+    if cache_params is not None:
+        cache_params.update_conv_state(F.pad(xbc_t, (self.conv_kernel_size - xbc_t.shape[-1], 0)), self.layer_idx)
+    conv = F.silu(self.conv1d(xbc_t)[..., :T].float()).to(dtype).transpose(1, 2).contiguous()   # [b, T, conv_dim]
+    x = conv[..., :I].view(b, T, H, P)
+    Bm, Cm = conv[..., I:I + GN], conv[..., I + GN:]
+    if st["R"] is not None:
+        if st["R"].device != conv.device:
+            st["R"] = st["R"].to(conv.device, torch.float32).contiguous()
+        Bm = rot_flat(Bm.reshape(b * T, GN), st["R"])
+        Cm = rot_flat(Cm.reshape(b * T, GN), st["R"])
+    A = -torch.exp(self.A_log.float())
+    lim = getattr(self, "time_step_limit", None)
+    lim = (0.0, math.inf) if lim is None else (float(lim[0]), float(lim[1]))
+    y, ssm = mamba_chunk_scan_combined(x, dt, A, Bm.reshape(b, T, G, N), Cm.reshape(b, T, G, N), self.chunk_size,
+                                       D=self.D, dt_bias=self.dt_bias, dt_softplus=True, dt_limit=lim,
+                                       return_final_states=True)
+    if cache_params is not None:
+        cache_params.update_recurrent_state(ssm, self.layer_idx)
+    scan_output = _norm(self, y.view(b, T, I), gate)
+    return self.out_proj(scan_output.to(self.out_proj.weight.dtype))
 
 
 def _dispatch(self, input_states, cache_params=None, attention_mask=None):
@@ -74,7 +132,11 @@ def _dispatch(self, input_states, cache_params=None, attention_mask=None):
     if (cache_params is not None and seq_len == 1 and st["pool"] is not None
             and cache_params.has_previous_state(self.layer_idx)):
         return _decode(self, input_states, cache_params)
-    out = st["orig"](self, input_states, cache_params, attention_mask)
+    if (seq_len > 1 and cache_params is not None and not cache_params.has_previous_state(self.layer_idx)
+            and st["lean_prefill"] and _lean_ok(self, input_states)):
+        out = _lean_prefill(self, input_states, cache_params, attention_mask)
+    else:
+        out = st["orig"](self, input_states, cache_params, attention_mask)
     if cache_params is not None:   # end of prefill: the tiered pool takes the final states
         ssm = cache_params.layers[self.layer_idx].recurrent_states.float()
         b, H, P, N = ssm.shape
@@ -89,11 +151,13 @@ def _dispatch(self, input_states, cache_params=None, attention_mask=None):
 
 
 def install(model, pb: int = 32, c: int = 16, cold: str | None = None, corr: int = 0, coldoff: int = 0,
-            cold_bf16: int | None = None) -> int:
+            cold_bf16: int | None = None, lean_prefill: int = 1) -> int:
     """Put the tiered decode into every NemotronH Mamba2 mixer of ``model``; returns how many.
 
     Argument names follow scale/v4_native_decode.py:247-256 (``cold_bf16=1`` means
-    ``cold="bf16"``, ``0`` means ``"fp32"``); ``cold="fp8"`` is the fp8 storage."""
+    ``cold="bf16"``, ``0`` means ``"fp32"``); ``cold="fp8"`` is the fp8 storage;
+    ``lean_prefill`` (default 1, as the reference's ``v4cfg.get("lean_prefill", 1)``) selects
+    the chunk-scan prefill."""
     if cold is None:
         cold = "fp32" if cold_bf16 == 0 else "bf16"
     mode = _MODES.get((int(bool(corr)), int(bool(coldoff))))
@@ -104,7 +168,7 @@ def install(model, pb: int = 32, c: int = 16, cold: str | None = None, corr: int
         if type(m).__name__ == "NemotronHMamba2Mixer":
             orig = type(m).torch_forward
             m._nssm = dict(pb=pb, c=c, cold=cold, mode=mode, pool=None, slots=None, orig=orig,
-                           R=_rotation_and_act(m))
+                           R=_rotation_and_act(m), lean_prefill=int(bool(lean_prefill)))
             m.torch_forward = _dispatch.__get__(m)
             n += 1
     return n

@@ -53,3 +53,71 @@ def test_hf_generate_matches_reference_install():
     assert torch.equal(out.sequences.cpu(), d["tokens"])
     for m in mixers:   # the decode went through the tiered pool
         assert m._nssm["pool"] is not None and int(m._nssm["pool"].t[0].max()) == cfg["new"] - 1
+
+
+def _bf16_model(seed: int):
+    """A small bf16 NemotronH whose mixers have the compiled chunk-scan shapes (headdim 80,
+    d_state 128, chunk 128), with seeded rotations wrapped around the activation."""
+    from transformers import NemotronHConfig, NemotronHForCausalLM
+    cfg = NemotronHConfig(hidden_size=128, num_hidden_layers=3, mamba_num_heads=8, mamba_head_dim=80,
+                          ssm_state_size=128, n_groups=2, vocab_size=100, hybrid_override_pattern="M*M",
+                          num_attention_heads=4, num_key_value_heads=2, head_dim=32, chunk_size=128)
+    torch.manual_seed(seed)
+    model = NemotronHForCausalLM(cfg).to(torch.bfloat16).eval()
+    Rs = GD.MG.hf_rotations(model, seed)
+    for m, R in zip([m for m in model.modules() if type(m).__name__ == "NemotronHMamba2Mixer"], Rs):
+        m.act = RotAct(m.act, m.intermediate_size, m.n_groups, m.ssm_state_size, R)
+    return model.cuda()
+
+
+def test_hf_lean_prefill_matches_torch_prefill():
+    """install(lean_prefill=1) runs the chunk scan for the prompt; on a one-chunk prompt (where
+    transformers' torch prefill is the exact recurrence) its logits agree with
+    install(lean_prefill=0) to the bf16 rounding of the two prefills, and the tiered pool holds
+    the scan's final state."""
+    from nested_ssm_b200 import materialize
+    from nested_ssm_b200.hf import install
+    g = torch.Generator().manual_seed(21)
+    ids = torch.randint(0, 100, (2, 100), generator=g).cuda()
+    outs = {}
+    for lean in (1, 0):
+        model = _bf16_model(16)
+        install(model, pb=32, c=4, cold_bf16=0, lean_prefill=lean)
+        with torch.no_grad():
+            out = model.generate(ids, max_new_tokens=3, do_sample=False, output_logits=True,
+                                 return_dict_in_generate=True, past_key_values=None)
+        outs[lean] = torch.stack(out.logits).float().cpu()
+        if lean:
+            mixers = [m for m in model.modules() if type(m).__name__ == "NemotronHMamba2Mixer"]
+            for m in mixers:
+                assert m._nssm["pool"] is not None
+    a, b = outs[1][0], outs[0][0]   # the logits of the prefill step
+    err = float((a - b).abs().max())
+    assert err <= 3e-2 * float(b.abs().max()) + 3e-2, f"lean vs torch prefill logits differ by {err}"
+
+
+def test_hf_lean_prefill_multi_chunk_runs():
+    """A 300-token prompt (three chunks) through the lean prefill: finite logits and the pool's
+    materialised state equals the fp32 state the scan left in the cache (fp32 cold)."""
+    from nested_ssm_b200 import materialize
+    from nested_ssm_b200.hf import install
+    g = torch.Generator().manual_seed(22)
+    ids = torch.randint(0, 100, (2, 300), generator=g).cuda()
+    model = _bf16_model(17)
+    install(model, pb=32, c=4, cold_bf16=0, lean_prefill=1)
+    captured = {}
+    mixers = [m for m in model.modules() if type(m).__name__ == "NemotronHMamba2Mixer"]
+    for m in mixers:
+        def hook(mod, args, kwargs, out, m=m):
+            cache = kwargs.get("cache_params", args[1] if len(args) > 1 else None)
+            if cache is not None and m._nssm["pool"] is not None and m.layer_idx not in captured:
+                captured[m.layer_idx] = cache.layers[m.layer_idx].recurrent_states.float().clone()
+        m.register_forward_hook(hook, with_kwargs=True)
+    with torch.no_grad():
+        out = model(ids, use_cache=True)
+    assert torch.isfinite(out.logits.float()).all()
+    for m in mixers:
+        st = m._nssm
+        full = materialize(st["pool"], 0, st["slots"], -torch.exp(m.A_log.float()))
+        torch.cuda.synchronize()
+        torch.testing.assert_close(full.cpu(), captured[m.layer_idx].cpu(), rtol=0, atol=0)

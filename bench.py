@@ -451,12 +451,18 @@ def time_prefill(args, rank: int, ws: int):
     flops = Bp * ((T + 127) // 128) * prefill_flops_per_chunk()
     gbs = nbytes / (ms / 1e3) / 1e9
     tfs = flops / (ms / 1e3) / 1e12
+    traffic = None
+    tr = (load_traffic() or {}).get("prefill_scan")
+    if tr:   # captured on a smaller case: scale by the bytes the two launches move
+        cap_bytes = tr["tokens"] * prefill_bytes_per_token() + tr["sequences"] * H * P * N * 4
+        traffic = int(tr["bytes_per_launch"] * nbytes / cap_bytes)
     return {"ms_per_launch": round(ms, 4), "tokens_per_s_per_layer": round(Bp * T / (ms / 1e3), 1),
             "tokens_per_s_27_layers": round(Bp * T / (27 * ms / 1e3), 1),
             "config": {"batch_per_gpu": Bp, "seqlen": T, "chunk_size": 128, "H": H, "P": P, "N": N, "G": G,
                        "dtype": "bf16 x/B/C/y, fp32 accumulate and state", "layout": "x/B/C views of conv output"},
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(gbs / peak, 4), "peak_kind": kind, "bytes_per_launch": nbytes,
+                         "traffic": traffic,
                          "tensor_tflops": round(tfs, 1), "tensor_frac": round(tfs / tflops_peak, 4),
                          "flops_per_launch": flops},
             "gpu_launches_per_layer": 1,

@@ -416,7 +416,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (it >= 2 && !wait_bar(&bar[B_CBFREE0 + s], (uint32_t)(((it >> 1) - 1) & 1), s_abort)) return false;
         tc_fence_after();
         const uint32_t cb = s ? kColCB1 : kColCB0;
-#pragma unroll
+#pragma unroll 1
         for (int kk = 0; kk < 8; ++kk) umma(tmem + cb, kdesc(st, kk), kdesc(st + kOp, kk), kIdCB, kk > 0);
         umma_commit(&bar[B_CBFULL0 + s]);
         return true;
@@ -432,7 +432,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (it > 0 && !wait_bar(&bar[B_SPFULL], pprev, s_abort)) break;
           if (it > 0 && !wait_bar(&bar[B_YOFREE], pprev, s_abort)) break;
           tc_fence_after();
-#pragma unroll
+#pragma unroll 1
           for (int kk = 0; kk < 8; ++kk)
             umma(tmem + kColYo, kdesc(sC, kk), sdesc(sSp + 256 * kk, 128, 2048), kIdY, kk > 0);
         }
@@ -442,13 +442,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         // S already holds exp(cs_last) * S_prev (the epilogue scaled it): accumulate the chunk.
         // Scaled B as the MN-major A operand (M = n): 128-byte swizzle, n halves 16 KB apart
         // (LBO), K groups of 8 token rows 1024 B apart (SBO)
-#pragma unroll
+#pragma unroll 1
         for (int kk = 0; kk < 8; ++kk)
           umma(tmem + kColS, sdesc(sB + 2048 * kk, 16384, 1024) | kSw128, xdesc(st, kk), kIdS, 1u);
         umma_commit(&bar[B_SFULL]);
         if (it > 0 && !wait_bar(&bar[B_YDFREE], pprev, s_abort)) break;
         tc_fence_after();
-#pragma unroll
+#pragma unroll 1
         for (int kk = 0; kk < 8; ++kk) umma(tmem + kColYd, sdesc(sM + 4096 * kk, 2048, 128), xdesc(st, kk), kIdY, kk > 0);
         umma_commit(&bar[B_YFULL]);
         umma_commit(&bar[B_MFREE]);
@@ -474,7 +474,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const float cs_l = v_cs[l];
       const uint32_t cb = (s ? kColCB1 : kColCB0) + ((uint32_t)(32 * q) << 16);
-#pragma unroll
+#pragma unroll 1
       for (int blk = 0; blk < 4; ++blk) {
         const int s0 = 64 * half + 16 * blk;
         uint4 w0 = make_uint4(0, 0, 0, 0), w1 = make_uint4(0, 0, 0, 0);
@@ -505,7 +505,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[B_CBFREE0 + s]);
       unsigned char* bt = stg + kOp;
-#pragma unroll
+#pragma unroll 1
       for (int k2 = 0; k2 < 8; ++k2) {
         // 16-byte chunk i of the swizzled tile holds 8 n of token row (i / 8) % 128
         const int i = a_idx + 256 * k2;
@@ -582,7 +582,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         eT1 = *(reinterpret_cast<const float*>(smem + L::kVec + vs1 * kVBytes) + 4 * kQ);
       }
       float* fin = p.fin ? p.fin + (int64_t)b * p.fin_sb + (int64_t)h * P * kN + erow : nullptr;
-#pragma unroll
+#pragma unroll 1
       for (int kb = 0; kb < NB0; ++kb) {
         if (kb < enb) {
           const int blk = eb0 + kb;

@@ -456,8 +456,9 @@ def time_prefill(args, rank: int, ws: int):
     if tr:   # captured on a smaller case: scale by the bytes the two launches move
         cap_bytes = tr["tokens"] * prefill_bytes_per_token() + tr["sequences"] * H * P * N * 4
         traffic = int(tr["bytes_per_launch"] * nbytes / cap_bytes)
-    return {"ms_per_launch": round(ms, 4), "tokens_per_s_per_layer": round(Bp * T / (ms / 1e3), 1),
-            "tokens_per_s_27_layers": round(Bp * T / (27 * ms / 1e3), 1),
+    # whole-job throughput: every rank scans its own prompt batch (max-over-ranks time)
+    return {"ms_per_launch": round(ms, 4), "tokens_per_s_per_layer": round(ws * Bp * T / (ms / 1e3), 1),
+            "tokens_per_s_27_layers": round(ws * Bp * T / (27 * ms / 1e3), 1), "n_gpus": ws,
             "config": {"batch_per_gpu": Bp, "seqlen": T, "chunk_size": 128, "H": H, "P": P, "N": N, "G": G,
                        "dtype": "bf16 x/B/C/y, fp32 accumulate and state", "layout": "x/B/C views of conv output"},
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",

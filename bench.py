@@ -54,6 +54,7 @@ def parse():
     ap.add_argument("--no-conv", action="store_true", help="skip the decode-token conv measurement")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--cpu-sample-batch", type=int, default=4)
+    ap.add_argument("--cpu-leg-only", action="store_true", help=argparse.SUPPRESS)
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of replaying CUDA graphs")
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill chunked-scan measurement")
     ap.add_argument("--prefill-only", action="store_true",
@@ -572,8 +573,33 @@ def cpu_sample(args, batch: int, steps: int, warmup: int, threads: int):
     return {"tokens_per_s": batch * steps / el, "step_s": times}
 
 
+def host_threads() -> int:
+    """Cores this process may run on (its CPU affinity; containers often allow fewer than
+    os.cpu_count() reports, and more torch threads than cores only slows the CPU legs)."""
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
+def cpu_baseline_leg_isolated(args):
+    """The CPU leg in a fresh interpreter: the bench process, after its GPU legs, runs the
+    same torch CPU code tens of times slower than a clean process does."""
+    cmd = [sys.executable, os.path.abspath(__file__), "--cpu-leg-only", "--layers", str(args.layers),
+           "--chunk", str(args.chunk), "--hot", str(args.hot), "--cold", args.cold,
+           "--cpu-sample-batch", str(args.cpu_sample_batch)]
+    env = dict(os.environ)
+    for k in ("RANK", "LOCAL_RANK", "WORLD_SIZE", "MASTER_ADDR", "MASTER_PORT"):
+        env.pop(k, None)
+    try:
+        out = subprocess.run(cmd, capture_output=True, text=True, timeout=600, env=env)
+        return json.loads(out.stdout.strip().splitlines()[-1])
+    except (subprocess.TimeoutExpired, ValueError, IndexError) as e:
+        return {"value": None, "unit": "tokens/s", "error": f"cpu leg failed: {type(e).__name__}"}
+
+
 def cpu_baseline_leg(args):
-    threads = os.cpu_count() or 1
+    threads = host_threads()
     r = cpu_sample(args, args.cpu_sample_batch, args.chunk, 1, threads)
     return {"value": round(r["tokens_per_s"], 3), "unit": "tokens/s", "cores": threads, "kind": "port",
             "sample": f"oracle (torch eager, {threads} threads): B={args.cpu_sample_batch} sequences x "
@@ -586,7 +612,7 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    threads = os.cpu_count() or 1
+    threads = host_threads()
     batch = args.cpu_sample_batch
     r = cpu_sample(args, batch, max(1, args.steps), max(0, min(args.warmup, 1)), threads)
     v = round(r["tokens_per_s"], 3)
@@ -609,6 +635,9 @@ def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.cpu_leg_only:
+        print(json.dumps(cpu_baseline_leg(args)), flush=True)
+        return 0
     rank, ws, local = dist_init()
     if not torch.cuda.is_available():
         raise SystemExit("bench.py needs a CUDA device")
@@ -709,7 +738,7 @@ def main():
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu:
-        cpu = cpu_baseline_leg(args)
+        cpu = cpu_baseline_leg_isolated(args)
 
     if rank == 0:
         line = {

@@ -62,6 +62,9 @@ def parse():
     ap.add_argument("--prefill-batch", type=int, default=64)
     ap.add_argument("--prefill-len", type=int, default=2048)
     ap.add_argument("--prefill-reps", type=int, default=0, help="timed launches (0: from --steps)")
+    ap.add_argument("--no-ragged", action="store_true", help="skip the continuous-batching ragged leg")
+    ap.add_argument("--ragged-slots", type=int, default=2048, help="slot pool per GPU of the ragged leg")
+    ap.add_argument("--ragged-steps", type=int, default=512, help="timed steps of the ragged leg")
     return ap.parse_args()
 
 
@@ -534,6 +537,148 @@ def time_e2e(wl: Workload, args, ws: int):
             "wall_ms_per_step": round((time.perf_counter() - t0) * 1e3 / K, 3)}
 
 
+def ragged_schedule(steps: int, rows: int, slots: int, seed: int, finish_p: float = 1.0 / 512,
+                    admit_p: float = 1.0 / 8, lo: int = 384, init: int = 416):
+    """Seeded continuous-batching admission process (host side, numpy).
+
+    A batch of `rows` positions holds live sequences (a pool slot each) or padding (-1).
+    Every step each live sequence finishes with probability `finish_p` (its slot returns
+    to the free list) and each empty position admits a new sequence with probability
+    `admit_p`, or always while fewer than `lo` are live.  Returns the per-step slot map
+    [steps, rows] and, per step, the slots admitted just before it (fresh state)."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    free = list(rng.permutation(slots))
+    cur = np.full(rows, -1, dtype=np.int32)
+    for r in rng.choice(rows, init, replace=False):
+        cur[r] = free.pop()
+    initial = cur[cur >= 0].copy()
+    sched = np.empty((steps, rows), dtype=np.int32)
+    admits = []
+    for k in range(steps):
+        new = []
+        if k > 0:
+            done = (cur >= 0) & (rng.random(rows) < finish_p)
+            free.extend(int(s) for s in cur[done])
+            cur[done] = -1
+            empty = np.flatnonzero(cur < 0)
+            take = empty[rng.random(empty.size) < admit_p]
+            need = lo - int((cur >= 0).sum())
+            if need > take.size:
+                take = np.union1d(take, empty[:need])
+            for r in take:
+                cur[r] = free.pop(0)
+                new.append(int(cur[r]))
+        sched[k] = cur
+        admits.append(np.array(new, dtype=np.int32))
+    return initial, sched, admits
+
+
+def time_ragged(args, rank: int, ws: int):
+    """Continuous-batching ragged decode (the BASELINE's slot-pool configuration): a pool of
+    `--ragged-slots` slots per GPU holding all 27 layers, 384-448 live sequences padded to 448
+    rows with slot -1, finishes and admissions every step, and per-slot flush phases (the
+    initial sequences start at token counts spread over 0..c-1; admitted ones at 0).  One
+    27-layer step is a CUDA graph reading the step's slot map from a device buffer;
+    admissions (prefill split of a fresh N(0, 0.1) state into every layer) run between
+    steps, outside the timed events.  tokens/s counts live rows only."""
+    from nested_ssm_b200 import TieredSlotPool, prefill_split, rot_flat, tiered_state_update
+    dev = torch.device("cuda")
+    L, Bm, S, c, K = args.layers, args.batch, args.ragged_slots, args.chunk, args.ragged_steps
+    W = max(3, args.warmup)
+    initial, sched, admits = ragged_schedule(W + K, Bm, S, seed=3000 + rank)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(3000 + rank)
+    pool = TieredSlotPool(L, S, H, P, N, G, args.hot, c, args.cold, torch.bfloat16, dev, max_batch=Bm)
+    A = [-torch.exp(torch.rand(H, device=dev, generator=gen) * math.log(16.0)) for _ in range(L)]
+    D = [torch.randn(H, device=dev, generator=gen) for _ in range(L)]
+    dtb = [torch.log(torch.expm1(torch.rand(H, device=dev, generator=gen) * (0.1 - 1e-3) + 1e-3)) for _ in range(L)]
+    R = [torch.linalg.qr(torch.randn(G, N, N, device=dev, generator=gen))[0].contiguous() for _ in range(L)]
+
+    def admit(slots_np):
+        if slots_np.size == 0:
+            return
+        sl = torch.from_numpy(slots_np).to(dev)
+        for l in range(L):
+            st = torch.randn(sl.numel(), H, P, N, device=dev, generator=gen) * math.sqrt(0.1)
+            prefill_split(pool, l, st, sl)
+
+    for i in range(0, initial.size, 64):
+        admit(initial[i:i + 64])
+    ini = torch.from_numpy(initial).long().to(dev)
+    pool.t[:, ini, :] = torch.randint(0, c, (ini.numel(), 1), device=dev, generator=gen).int()
+    NI = Workload.NI
+    x = torch.randn(NI, L, Bm, H, P, device=dev, generator=gen).to(torch.bfloat16)
+    dt = torch.randn(NI, L, Bm, H, device=dev, generator=gen).to(torch.bfloat16)
+    BC = (torch.randn(NI, L, 2 * Bm, G * N, device=dev, generator=gen) / math.sqrt(N)).to(torch.bfloat16)
+    BCr = torch.empty(2 * Bm, G * N, dtype=torch.bfloat16, device=dev)
+    y = torch.empty(L, Bm, H, P, dtype=torch.bfloat16, device=dev)
+    sched_d = torch.from_numpy(sched).to(dev)
+    slots = torch.empty(Bm, dtype=torch.int32, device=dev)
+
+    def one_step(i):
+        for l in range(L):
+            rot_flat(BC[i, l], R[l], out=BCr)
+            tiered_state_update(pool, l, x[i, l], dt[i, l], A[l], BCr[:Bm].view(Bm, G, N), BCr[Bm:].view(Bm, G, N),
+                                D[l], dtb[l], True, slots, -1, y[l], None, 1e-3)
+
+    graphs = None
+    if not args.no_graph:
+        graphs = []
+        cap = torch.cuda.Stream()
+        slots.copy_(sched_d[0])
+        for i in range(NI):
+            one_step(i)   # warm every input set once before capture
+        torch.cuda.synchronize()
+        for i in range(NI):
+            g = torch.cuda.CUDAGraph()
+            cap.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(cap):
+                with torch.cuda.graph(g, stream=cap):
+                    one_step(i)
+            torch.cuda.current_stream().wait_stream(cap)
+            graphs.append(g)
+        torch.cuda.synchronize()
+        # the warm-up steps above advanced the token counts of the initial sequences; that
+        # only shifts their phases
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    live = 0
+    for k in range(W + K):
+        admit(admits[k])
+        slots.copy_(sched_d[k])
+        timed = k >= W
+        if timed:
+            evs[k - W][0].record()
+        if graphs is not None:
+            graphs[k % NI].replay()
+        else:
+            one_step(k % NI)
+        if timed:
+            evs[k - W][1].record()
+            live += int((sched[k] >= 0).sum())
+    torch.cuda.synchronize()
+    pool.check_status()
+    tot_ms = sum(a.elapsed_time(b) for a, b in evs)
+    ms = max_over_ranks(tot_ms, ws)
+    live_all = live
+    if ws > 1:
+        import torch.distributed as dist
+        t = torch.tensor([live], dtype=torch.float64, device=dev)
+        dist.all_reduce(t)
+        live_all = int(t.item())
+    ph = (pool.t[0, torch.from_numpy(sched[-1][sched[-1] >= 0]).long().to(dev), 0] % c).bincount(minlength=c)
+    del graphs
+    return {"tokens_per_s": round(live_all / (ms / 1e3), 1), "ms_per_step": round(ms / K, 4), "steps": K,
+            "warmup": W, "live_rows_per_step": round(live / K, 1), "padded_batch": Bm, "slots_per_gpu": S,
+            "layers": L, "chunk": c, "n_gpus": ws, "admitted": int(sum(a.size for a in admits[W:])),
+            "flush_phase_histogram_last_step": [int(v) for v in ph.tolist()],
+            "config": "continuous batching: finish p=1/512, admit p=1/8 per empty row, >=384 live, "
+                      "padded to 448 with slot -1, per-slot flush phases; pool of %d slots x %d layers "
+                      "(%.1f GB; the configuration's 4096 slots x 27 layers exceed HBM)"
+                      % (S, L, L * S * bytes_per_slot(args) / 1e9),
+            "gpu_launches_per_step": L * 3}
+
+
 # --------------------------------------------------------------------------
 # CPU legs (the oracle port -- the reference's own path is Python/torch)
 # --------------------------------------------------------------------------
@@ -735,6 +880,8 @@ def main():
     fresh = None if args.no_fresh else time_fresh(args, rank, ws)
     conv = None if args.no_conv else time_conv(args, rank, ws)
     prefill = None if args.no_prefill else time_prefill(args, rank, ws)
+    torch.cuda.empty_cache()
+    ragged = None if args.no_ragged else time_ragged(args, rank, ws)
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu:
@@ -760,6 +907,7 @@ def main():
             "speedup_vs_fresh": round(value / fresh["tokens_per_s"], 3) if fresh else None,
             "conv_step": conv,
             "prefill_scan": prefill,
+            "ragged": ragged,
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)

@@ -303,7 +303,27 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
   int* btn = reinterpret_cast<int*>(sm + L.off_bmeta);   // token count after this step
   int* bpos = reinterpret_cast<int*>(sm + L.off_bpos);   // ring position of this token, -(pos+1) if it flushes
 
-  const int W = pp.items;
+  // FLUSH works on the rows at a chunk boundary only, numbered in batch order (every CTA
+  // repeats the count from the token counts STEP wrote); their items are split evenly over
+  // the grid, so a batch whose rows flush on different tokens (per-slot phases) spreads
+  // each token's flushes over every SM.  Rows b0.. below are such compacted rows in FLUSH
+  // and batch rows in STEP.
+  const int batch = pp.items / H;
+  auto flush_row = [&](int b, int& slot, int& tn) -> bool {
+    slot = p.idx ? p.idx[b] : b;
+    if (slot == p.pad || slot < 0 || slot >= p.S) return false;
+    tn = p.t[(int64_t)slot * H];
+    return tn > 0 && tn % c == 0;
+  };
+  int W = pp.items;
+  if constexpr (!STEP) {
+    int nfl = 0;
+    for (int c0 = 0; c0 < batch; c0 += kPT) {
+      int sl = -1, tn = 0;
+      nfl += __syncthreads_count(c0 + tid < batch && flush_row(c0 + tid, sl, tn));
+    }
+    W = nfl * H;
+  }
   const int beg = (int)((long long)W * blockIdx.x / gridDim.x);
   const int end = (int)((long long)W * (blockIdx.x + 1) / gridDim.x);
   if (beg >= end) return;
@@ -311,22 +331,50 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
   const int nb = (end - 1) / H - b0 + 1;
   const int nit = end - beg;
 
-  // ---- prologue 1: slot and token count after this step of every batch row in
-  // range.  STEP reads t and adds one; FLUSH reads the count STEP wrote and keeps
-  // only the rows that flush.
+  // ---- prologue 1: slot and token count after this step of every row in range.  STEP
+  // reads t and adds one; FLUSH takes the flushing rows numbered b0 .. b0 + nb - 1 (a
+  // block-wide exclusive count by warp ballots).
   bool any = false;
-  for (int j = tid; j < nb; j += kPT) {
+  if constexpr (!STEP) {
+    int* wcnt = reinterpret_cast<int*>(sm + L.off_pc);   // per-warp counts (pc is free here)
+    int base = 0;
+    for (int c0 = 0; c0 < batch && base < b0 + nb; c0 += kPT) {   // uniform over the CTA
+      const int b = c0 + tid;
+      int slot = -1, tn = 0;
+      const bool f = b < batch && flush_row(b, slot, tn);
+      const unsigned bal = __ballot_sync(0xffffffffu, f);
+      if (lane == 0) wcnt[warp] = __popc(bal);
+      __syncthreads();
+      int pre = 0, tot = 0;
+      for (int w = 0; w < kPW; ++w) {
+        const int n = wcnt[w];
+        pre += w < warp ? n : 0;
+        tot += n;
+      }
+      if (f) {
+        const int pos = base + pre + __popc(bal & ((1u << lane) - 1u));
+        if (pos >= b0 && pos < b0 + nb) {
+          bslot[pos - b0] = slot;
+          btn[pos - b0] = tn;
+          bpos[pos - b0] = -c;
+        }
+      }
+      base += tot;
+      __syncthreads();
+    }
+    any = true;
+  }
+  for (int j = tid; STEP && j < nb; j += kPT) {
     const int b = b0 + j;
     const int slot = p.idx ? p.idx[b] : b;
     int s = -1, tn = 0;
     if (slot != p.pad) {
       if (slot < 0 || slot >= p.S) {
-        if (STEP && p.status) atomicOr(p.status, STATUS_BAD_SLOT);
+        if (p.status) atomicOr(p.status, STATUS_BAD_SLOT);
       } else {
         const int hf = (j == 0) ? beg - b0 * H : 0;   // first head of row b owned here
         s = slot;
-        tn = p.t[(int64_t)slot * H + hf] + (STEP ? 1 : 0);
-        if (!STEP && (tn <= 0 || tn % c != 0)) s = -1;   // FLUSH: only flushing rows
+        tn = p.t[(int64_t)slot * H + hf] + 1;
       }
     }
     any |= s >= 0;
@@ -335,8 +383,9 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
     const int ps = tn > 0 ? (tn - 1) % c : 0;
     bpos[j] = (ps == c - 1) ? -(ps + 1) : ps;
   }
-  // nothing to do in this CTA's range (every row padded, or, in FLUSH, no row at a chunk
-  // boundary -- the FLUSH launch of c - 1 tokens out of c): leave before any set-up
+  // nothing to do in this CTA's range (STEP: every row padded; FLUSH left above when no
+  // row of the batch is at a chunk boundary -- c - 1 launches out of c in lockstep
+  // batches): leave before any set-up
   if (!__syncthreads_or(any)) return;
   if (!STEP) {
     for (int h = tid; h < H; h += kPT) sA[h] = p.A[h];

@@ -167,6 +167,33 @@ def test_ragged_pad_and_phase_offsets():
     assert int(gpool.status.item()) == 0
 
 
+def test_flush_rows_spread_over_grid():
+    """Rows join on different tokens, so on every token a different quarter of the batch
+    (interleaved rows) is at a chunk boundary.  FLUSH numbers those rows and splits only
+    their items over the whole grid: 16 flushing rows x 128 heads land on hundreds of CTAs
+    whose item ranges start and end inside rows."""
+    from nested_ssm_b200 import prefill_split
+    b, S, c, steps = 64, 80, 4, 10
+    case = Hh.make_case(b=b, S=S, pb=32, c=c, cold="fp8", steps=steps, seed=21)
+    opool, gpool = Hh.oracle_pool(case), Hh.gpu_pool(case)
+    all_slots = torch.randperm(S, generator=torch.Generator().manual_seed(21))[:b]
+    join = torch.arange(b) % c   # row r joins on step r % c
+    for s in range(steps):
+        idx = (join == s).nonzero().flatten()
+        if idx.numel():
+            O.prefill_split(opool, all_slots[idx], case["state0"][idx])
+            prefill_split(gpool, 0, case["state0"][idx].cuda(), all_slots[idx].to(torch.int32).cuda())
+        live = join <= s
+        slots = torch.where(live, all_slots, torch.full_like(all_slots, -1))
+        Hh.sync_oracle_from_gpu(gpool, opool)   # every token from identical state: the per-step bar
+        yg, yo = Hh.step_both(case, gpool, opool, s, slots)
+        Hh.assert_y_close(yg, yo, f"step {s}")
+        Hh.compare_pool(gpool, opool, 0, all_slots, "fp8", max_ulp=1, max_ulp_frac=1e-4)
+        if s >= c - 1:   # exactly one quarter of the rows flushed on this token
+            assert int((opool.t[all_slots[live]] % c == 0).sum()) == b // c
+    assert int(gpool.status.item()) == 0
+
+
 @pytest.mark.parametrize("mode", ["corr", "coldoff"])
 def test_modes(mode):
     case = Hh.make_case(b=4, S=4, pb=32, c=4, cold="fp32", steps=9, seed=5)

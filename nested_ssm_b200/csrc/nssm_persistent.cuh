@@ -281,7 +281,7 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int c = CFIX > 0 ? CFIX : p.c;
-  const int Pn = p.P;
+  const int Pn = RPWC > 0 ? kPW * RPWC : p.P;   // the RPWC instances run only for headdim == 8 * RPWC
   const int H = p.H;
   const int cp = ring_dt_stride(c);
   const int HG = H / p.G;

@@ -5,12 +5,14 @@
 // FLUSH on the same stream; FLUSH finds its work from the token counts STEP wrote.
 //
 // Grid = (#SMs x resident CTAs).  CTA k owns the contiguous range of work items
-// [k*W/G, (k+1)*W/G) over (batch row, head), W = batch*H, so it streams the tiles of
-// consecutive heads of the same slot.
+// [k*W/G, (k+1)*W/G) over (row, head), so it streams the tiles of consecutive heads of
+// the same slot.  STEP: rows are the batch rows, W = batch*H.  FLUSH: rows are the batch
+// rows at a chunk boundary, numbered in batch order, W = (their count)*H.
 //
-// Prologue (once per CTA): the slot and token count of every batch row in range and
-// (STEP) every item's scalars (dt = softplus(dt_raw + dt_bias) clamped, dt*A,
-// exp(dt*A), exp(glog), D) are computed in parallel into shared memory.
+// Prologue (once per CTA): the slot and token count of every row in range and (STEP)
+// every item's scalars (dt = softplus(dt_raw + dt_bias) clamped, dt*A, exp(dt*A),
+// exp(glog), D) or (FLUSH) every item's suffix decays are computed in parallel into
+// shared memory.
 //
 // Main loop: one elected thread keeps kStages items in flight with 1-D bulk copies
 // (cp.async.bulk global->shared, no multicast) completing on a "full" mbarrier per

@@ -141,12 +141,18 @@ int launch_rot(const nssm::RotParams& rp, int rows_total, int G, cudaStream_t st
   const unsigned long long bit = 1ull << (dev & 63);
   constexpr int smem = nssm::rot_smem_bytes(128);
   if (!(attr_done.load(std::memory_order_acquire) & bit)) {
-    if (cudaFuncSetAttribute(nssm::rot_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    if (cudaFuncSetAttribute(nssm::rot_kernel<128, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(nssm::rot_kernel<128, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+            cudaSuccess)
       return cuda_check("cudaFuncSetAttribute(rot_kernel)");
     attr_done.fetch_or(bit, std::memory_order_acq_rel);
   }
   dim3 grid((unsigned)((rows_total + nssm::kRotTile - 1) / nssm::kRotTile), (unsigned)G, 128 / nssm::kRotHalf);
-  nssm::rot_kernel<128><<<grid, nssm::kRotThreads, smem, st>>>(rp, rows_total);
+  if (rp.dtype == NSSM_BF16)
+    nssm::rot_kernel<128, true><<<grid, nssm::kRotThreads, smem, st>>>(rp, rows_total);
+  else
+    nssm::rot_kernel<128, false><<<grid, nssm::kRotThreads, smem, st>>>(rp, rows_total);
   return cuda_check("rot_kernel launch");
 }
 

@@ -29,7 +29,19 @@ constexpr int kRotLd = 132;   // padded row length: 16-byte aligned, rows 4 bank
 
 __host__ __device__ constexpr int rot_smem_bytes(int N) { return (kRotHalf + kRotTile) * kRotLd * 4; }
 
-template <int N>
+// io values as fp32 / back, the io dtype fixed at compile time (bf16 or fp32)
+template <bool IOBF>
+__device__ __forceinline__ float rot_ld(const void* p, int64_t i) {
+  if constexpr (IOBF) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+  else return reinterpret_cast<const float*>(p)[i];
+}
+template <bool IOBF>
+__device__ __forceinline__ void rot_st(void* p, int64_t i, float v) {
+  if constexpr (IOBF) reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+  else reinterpret_cast<float*>(p)[i] = v;
+}
+
+template <int N, bool IOBF>
 __global__ void __launch_bounds__(kRotThreads, 4) rot_kernel(const RotParams p, int rows_total) {
   static_assert(N == 128, "tile mapping assumes dstate 128");
   extern __shared__ __align__(16) float rsm[];
@@ -68,7 +80,7 @@ __global__ void __launch_bounds__(kRotThreads, 4) rot_kernel(const RotParams p, 
       const int64_t base = (int64_t)(second ? j - p.T : j) * (second ? p.xs1 : p.xs0) + (int64_t)g * N;
 #pragma unroll
       for (int t = 0; t < 4; ++t)
-        v[u][t] = r < nr ? ld_io(x, base + lane + 32 * t, p.dtype) : 0.0f;   // strides may be odd
+        v[u][t] = r < nr ? rot_ld<IOBF>(x, base + lane + 32 * t) : 0.0f;   // strides may be odd
     }
 #pragma unroll
     for (int u = 0; u < kRowsPerWarp; ++u)
@@ -113,7 +125,7 @@ __global__ void __launch_bounds__(kRotThreads, 4) rot_kernel(const RotParams p, 
     void* o = second ? p.o1 : p.o0;
     const int64_t ob = (int64_t)row * (second ? p.os1 : p.os0) + (int64_t)g * N + m0;
 #pragma unroll
-    for (int jj = 0; jj < 4; ++jj) st_io(o, ob + mg + 16 * jj, p.dtype, acc[i][jj]);
+    for (int jj = 0; jj < 4; ++jj) rot_st<IOBF>(o, ob + mg + 16 * jj, acc[i][jj]);
   }
 }
 

@@ -1,0 +1,34 @@
+"""The continuous-batching admission process of bench.py's ragged leg (host side, CPU).
+
+Seeded and reproducible; 384-448 live sequences in a padded batch of 448 rows; a slot is
+never live in two rows at once and is only reused after its sequence finished; admitted
+slots are exactly the rows that change from padding or another slot.
+"""
+import numpy as np
+
+import bench
+
+
+def test_ragged_schedule_invariants():
+    rows, slots, steps = 448, 2048, 700
+    initial, sched, admits = bench.ragged_schedule(steps, rows, slots, seed=3000)
+    again = bench.ragged_schedule(steps, rows, slots, seed=3000)
+    assert np.array_equal(sched, again[1]) and np.array_equal(initial, again[0])
+    live = (sched >= 0).sum(axis=1)
+    assert live.min() >= 384 and live.max() <= rows
+    assert sched.max() < slots and sched.min() >= -1
+    assert set(initial.tolist()) == set(sched[0][sched[0] >= 0].tolist())
+    finished = set()
+    prev = sched[0]
+    for k in range(1, steps):
+        cur = sched[k]
+        ids = cur[cur >= 0]
+        assert len(set(ids.tolist())) == ids.size, f"step {k}: a slot sits in two rows"
+        changed = (cur != prev) & (cur >= 0)
+        assert sorted(cur[changed].tolist()) == sorted(admits[k].tolist()), f"step {k}: admissions"
+        gone = set(prev[(prev >= 0) & (cur != prev)].tolist())
+        finished |= gone
+        for s in admits[k].tolist():
+            assert s not in set(prev[prev >= 0].tolist()), f"step {k}: slot {s} admitted while live"
+        prev = cur
+    assert sum(a.size for a in admits) > 0 and len(finished) > 0

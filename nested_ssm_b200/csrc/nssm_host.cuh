@@ -94,7 +94,7 @@ inline int launch_phase(const nssm::StepParams& sp, int batch, cudaStream_t st, 
 }
 
 // Both phases of one step.  The production configuration (fp8 cold, bf16 io) has
-// instances compiled for c in {4, 8, 16} and headdim in {64, 80}; anything else
+// instances compiled for c in {4, 8, 16, 64} and headdim in {64, 80}; anything else
 // runs the instances that read c and headdim at run time.
 template <int PB, int NC, int COLD, bool IOBF, int CFIX, int RPWC>
 inline int launch_both(const nssm::StepParams& sp, int batch, cudaStream_t st, bool ring_ok, int sms) {
@@ -114,6 +114,7 @@ inline int launch_c(const nssm::StepParams& sp, int batch, cudaStream_t st, bool
     case 4: return launch_both<PB, NC, COLD, IOBF, 4, RPWC>(sp, batch, st, ring_ok, sms);
     case 8: return launch_both<PB, NC, COLD, IOBF, 8, RPWC>(sp, batch, st, ring_ok, sms);
     case 16: return launch_both<PB, NC, COLD, IOBF, 16, RPWC>(sp, batch, st, ring_ok, sms);
+    case 64: return launch_both<PB, NC, COLD, IOBF, 64, RPWC>(sp, batch, st, ring_ok, sms);
   }
   return launch_both<PB, NC, COLD, IOBF, 0, 0>(sp, batch, st, ring_ok, sms);
 }

@@ -721,23 +721,37 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
       // exp(suf_j) [c], dt_j [c], exp(total): the prologue's table, or computed per warp
       const float* dec = pre ? reinterpret_cast<const float*>(sm + L.off_fsc) + (b * H + h - beg) * (2 * c + 1)
                              : wsc;
-      if (!pre && lane == 0) {   // suffix decays (per warp; identical in every warp)
-        float tot = 0.0f;
-        for (int j = 0; j < c; ++j) tot = tot + ring_dt_at(j) * A_h;
-        wsc[2 * c] = expf(tot);
-        wsc[c - 1] = 1.0f;
-        wsc[c + c - 1] = ring_dt_at(c - 1);
-        float suf = 0.0f;
-        for (int j = c - 2; j >= 0; --j) {
-          suf = suf + ring_dt_at(j + 1) * A_h;
-          wsc[j] = expf(suf);
-          wsc[c + j] = ring_dt_at(j);
+      if (!pre) {   // suffix decays (per warp; identical in every warp)
+        // the c dts loaded by all lanes at once, the sums in j order by one lane, the
+        // exponentials by all lanes again
+        for (int j = lane; j < c; j += 32) wsc[c + j] = ring_dt_at(j);
+        __syncwarp();
+        if (lane == 0) {
+          float tot = 0.0f;
+          for (int j = 0; j < c; ++j) tot = tot + wsc[c + j] * A_h;
+          wsc[2 * c] = expf(tot);
+          float suf = 0.0f;
+          for (int j = c - 2; j >= 0; --j) {
+            suf = suf + wsc[c + j + 1] * A_h;
+            wsc[j] = suf;
+          }
         }
+        __syncwarp();
+        for (int j = lane; j < c - 1; j += 32) wsc[j] = expf(wsc[j]);
+        if (lane == 0) wsc[c - 1] = 1.0f;
+        __syncwarp();
       }
-      if (!pre) __syncwarp();
-      // W_j[row] = exp(suf_j) * (dt_j * x_j[row]) for the band's rows
-      for (int j = 0; j < c; ++j) {
-        if (lane < nrow) sW[j * Pn + r0 + lane] = __fmul_rn(dec[j], __fmul_rn(dec[c + j], ring_x_at(j, r0 + lane)));
+      // W_j[row] = exp(suf_j) * (dt_j * x_j[row]) for the band's rows; past kRingF32Max tokens
+      // every (j, row) pair of the band goes over the lanes, so the ring loads are independent
+      if (pre) {
+        for (int j = 0; j < c; ++j) {
+          if (lane < nrow) sW[j * Pn + r0 + lane] = __fmul_rn(dec[j], __fmul_rn(dec[c + j], ring_x_at(j, r0 + lane)));
+        }
+      } else {
+        for (int i = lane; i < c * nrow; i += 32) {
+          const int j = i / nrow, r = r0 + (i - j * nrow);
+          sW[j * Pn + r] = __fmul_rn(dec[j], __fmul_rn(dec[c + j], ring_x_at(j, r)));
+        }
       }
       __syncwarp();
       const float etot = dec[2 * c];

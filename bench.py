@@ -13,6 +13,12 @@ L2 flush is needed between steps.
 
 N > 1 runs under torchrun: every rank owns its own slot pool and batch of 448
 (weak scaling, no data-path collective).
+
+Besides the headline step the line carries: `e2e` (the same step through the public API
+with host copies), `cpu_baseline` (the oracle port on the host cores), `fresh_control`
+(the untiered fp32 update), `conv_step`, `prefill_scan` (the chunked prefill scan) and
+`ragged` (a continuous-batching run over a slot pool with finishes, admissions and per-slot
+flush phases); `--no-<leg>` skips one.
 """
 from __future__ import annotations
 

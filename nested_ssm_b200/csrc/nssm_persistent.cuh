@@ -309,7 +309,8 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
   // repeats the count from the token counts STEP wrote); their items are split evenly over
   // the grid, so a batch whose rows flush on different tokens (per-slot phases) spreads
   // each token's flushes over every SM.  Rows b0.. below are such compacted rows in FLUSH
-  // and batch rows in STEP.
+  // and batch rows in STEP.  The count costs every CTA two loads per batch row (slot, then
+  // its token count): two passes of 256 rows at B=448.
   const int batch = pp.items / H;
   auto flush_row = [&](int b, int& slot, int& tn) -> bool {
     slot = p.idx ? p.idx[b] : b;

@@ -94,7 +94,7 @@ def step_bytes_per_seq(c: int, pb: int, cold: str, io_bytes: int = 2, out_bytes:
     return step + flush / c
 
 
-def survey_bytes_per_seq(c: int) -> float:
+def reference_model_bytes_per_seq(c: int) -> float:
     """Byte model the reference's design implies (separate flush, fp32 ring)."""
     return 3_780_872 + 2_048_000 / c
 
@@ -882,7 +882,7 @@ def main():
         roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
                 "kernel": "tiered state update (STEP + FLUSH persistent kernels)", "kernel_ms_avg": round(kms, 4),
-                "bytes_per_launch": int(B * bps), "survey_bytes_per_launch": int(B * survey_bytes_per_seq(args.chunk)),
+                "bytes_per_launch": int(B * bps), "reference_model_bytes_per_launch": int(B * reference_model_bytes_per_seq(args.chunk)),
                 "rotation_ms_avg": round(statistics.mean(rd_all), 4) if rd_all else None,
                 "kernel_ms_by_step": [round(statistics.mean(kd_all[i * L:(i + 1) * L]), 4)
                                       for i in range(len(kd_all) // L)],

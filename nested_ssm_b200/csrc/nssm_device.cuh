@@ -324,7 +324,7 @@ __global__ void __launch_bounds__(128 * TPR, (TPR == 2 ? NSSM_STEP_MINB : NSSM_F
   const int g = h / HG;
   const int64_t sh = (int64_t)slot * p.H + h;   // (slot, head)
 
-  // ---- memory round 1: the tile and every small input, issued together
+  // ---- first batch of loads: the tile and every small input, issued together
   const int nh = Pn * LPR;
   const int hcol = tid % LPR;
   float4* hot4 = reinterpret_cast<float4*>(p.hot + sh * (int64_t)Pn * PB);

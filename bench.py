@@ -553,6 +553,9 @@ def ragged_schedule(steps: int, rows: int, slots: int, seed: int, finish_p: floa
     `admit_p`, or always while fewer than `lo` are live.  Returns the per-step slot map
     [steps, rows] and, per step, the slots admitted just before it (fresh state)."""
     import numpy as np
+    if slots <= rows or not 0 < lo <= init <= rows:
+        raise ValueError(f"ragged schedule needs slots > rows >= init >= lo > 0 "
+                         f"(slots {slots}, rows {rows}, init {init}, lo {lo})")
     rng = np.random.default_rng(seed)
     free = list(rng.permutation(slots))
     cur = np.full(rows, -1, dtype=np.int32)

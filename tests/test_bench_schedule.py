@@ -5,6 +5,7 @@ never live in two rows at once and is only reused after its sequence finished; a
 slots are exactly the rows that change from padding or another slot.
 """
 import numpy as np
+import pytest
 
 import bench
 
@@ -32,3 +33,8 @@ def test_ragged_schedule_invariants():
             assert s not in set(prev[prev >= 0].tolist()), f"step {k}: slot {s} admitted while live"
         prev = cur
     assert sum(a.size for a in admits) > 0 and len(finished) > 0
+
+
+def test_ragged_schedule_rejects_a_pool_no_larger_than_the_batch():
+    with pytest.raises(ValueError, match="slots > rows"):
+        bench.ragged_schedule(4, 448, 448, seed=0)

@@ -120,7 +120,7 @@ def test_config0_fp32_64_steps_with_rotation():
     Hh.compare_pool(gpool, opool, 0, slots, "fp32", hot_rtol=1e-4, hot_atol=1e-5)
 
 
-@pytest.mark.parametrize("c,P", [(2, 80), (8, 80), (16, 80), (64, 80), (4, 64), (8, 64), (16, 64), (4, 48)])
+@pytest.mark.parametrize("c,P", [(2, 80), (8, 80), (16, 80), (64, 80), (4, 64), (8, 64), (16, 64), (64, 64), (4, 48)])
 def test_chunk_and_headdim_instances(c, P):
     """The production configuration (fp8 cold, bf16 io) has kernels with c and
     headdim fixed at compile time (c in {4, 8, 16, 64}, headdim in {64, 80}); the others

@@ -71,6 +71,11 @@ def parse():
     ap.add_argument("--no-ragged", action="store_true", help="skip the continuous-batching ragged leg")
     ap.add_argument("--ragged-slots", type=int, default=2048, help="slot pool per GPU of the ragged leg")
     ap.add_argument("--ragged-steps", type=int, default=512, help="timed steps of the ragged leg")
+    ap.add_argument("--no-config1", action="store_true", help="skip the B=256 / 256-step configuration")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="skip the same-box run of the reference's own GPU decode arms")
+    ap.add_argument("--reference-gpu-leg-only", action="store_true", help=argparse.SUPPRESS)
+    ap.add_argument("--no-multi-gpu-check", action="store_true")
     return ap.parse_args()
 
 
@@ -480,17 +485,60 @@ def time_prefill(args, rank: int, ws: int):
             "kernel": "chunk_scan_kernel (tcgen05: C.B^T, C.S_prev, M.x, B_s^T.x per 128-token chunk)"}
 
 
-def time_e2e(wl: Workload, args, ws: int):
+def gpu_local_cpus(device_index: int) -> list[int] | None:
+    """Host CPUs on the GPU's NUMA node (sysfs ``local_cpulist`` of its PCI device), or None
+    when the platform does not say."""
+    try:
+        pr = torch.cuda.get_device_properties(device_index)
+        path = "/sys/bus/pci/devices/%04x:%02x:%02x.0/local_cpulist" % (pr.pci_domain_id, pr.pci_bus_id,
+                                                                      pr.pci_device_id)
+        with open(path) as f:
+            txt = f.read().strip()
+    except (OSError, AttributeError, RuntimeError):
+        return None
+    cpus = []
+    for part in txt.split(","):
+        if "-" in part:
+            a, b = part.split("-")
+            cpus.extend(range(int(a), int(b) + 1))
+        elif part:
+            cpus.append(int(part))
+    allowed = os.sched_getaffinity(0)
+    cpus = [c for c in cpus if c in allowed]
+    return cpus or None
+
+
+def pinned_near_gpu(tensors, device_index: int):
+    """Pinned host copies of ``tensors`` whose pages are first touched by a thread running on
+    the GPU's own NUMA node (the kernel places pages where they are first written)."""
+    cpus = gpu_local_cpus(device_index)
+    old = os.sched_getaffinity(0)
+    try:
+        if cpus:
+            os.sched_setaffinity(0, cpus)
+        return [t.cpu().pin_memory() if t.is_cuda else t.pin_memory() for t in tensors], cpus
+    finally:
+        os.sched_setaffinity(0, old)
+
+
+def e2e_steps(args) -> int:
+    """Timed steps of the e2e leg: whole c-token cycles (every window of k*c consecutive
+    tokens holds exactly k flush tokens of a lockstep batch), at least 8 and about half of
+    --steps."""
+    c = args.chunk
+    return c * max(1, -(-max(8, args.steps // 2) // c))
+
+
+def time_e2e(wl: Workload, args, ws: int, local: int):
     """Same metric through the public API with HOST buffers: every step copies that
     step's inputs (x, dt, B, C of all layers) from pinned host memory and reads y
-    back; copies overlap compute on separate streams, layer by layer."""
+    back; copies overlap compute on separate streams, layer by layer.  The timed window is
+    whole c-token cycles.  A second run moves the same bytes with no compute (the host
+    copy ceiling of this GPU with every rank copying at once)."""
     from nested_ssm_b200 import rot_flat, tiered_state_update
     L, B = wl.L, wl.B
-    dev = torch.device("cuda")
-    hx = wl.x[0].cpu().pin_memory()
-    hdt = wl.dt[0].cpu().pin_memory()
-    hBC = wl.BC[0].cpu().pin_memory()
-    hy = torch.empty(L, B, H, P, dtype=torch.bfloat16).pin_memory()
+    (hx, hdt, hBC), numa_cpus = pinned_near_gpu([wl.x[0], wl.dt[0], wl.BC[0]], local)
+    (hy,), _ = pinned_near_gpu([torch.empty(L, B, H, P, dtype=torch.bfloat16)], local)
     dx = torch.empty_like(wl.x[0])
     ddt = torch.empty_like(wl.dt[0])
     dBC = torch.empty_like(wl.BC[0])
@@ -502,7 +550,7 @@ def time_e2e(wl: Workload, args, ws: int):
     h2d = (hx.numel() * hx.element_size() + hdt.numel() * hdt.element_size() + hBC.numel() * hBC.element_size())
     d2h = hy.numel() * hy.element_size()
 
-    def step():
+    def step(compute=True):
         for l in range(L):
             with torch.cuda.stream(s_in):
                 if not first[0]:
@@ -512,55 +560,77 @@ def time_e2e(wl: Workload, args, ws: int):
                 dBC[l].copy_(hBC[l], non_blocking=True)
                 ev_in[l].record(s_in)
             comp.wait_event(ev_in[l])
-            rot_flat(dBC[l], wl.R[l], out=wl.BCr)
-            tiered_state_update(wl.pool, l, dx[l], ddt[l], wl.A[l], wl.BCr[:B].view(B, G, N),
-                                wl.BCr[B:].view(B, G, N), wl.D[l], wl.dtb[l], True, wl.slots, -1, wl.y[l],
-                                None, 1e-3)
+            if compute:
+                rot_flat(dBC[l], wl.R[l], out=wl.BCr)
+                tiered_state_update(wl.pool, l, dx[l], ddt[l], wl.A[l], wl.BCr[:B].view(B, G, N),
+                                    wl.BCr[B:].view(B, G, N), wl.D[l], wl.dtb[l], True, wl.slots, -1, wl.y[l],
+                                    None, 1e-3)
             ev_done[l].record(comp)
             with torch.cuda.stream(s_out):
                 s_out.wait_event(ev_done[l])
                 hy[l].copy_(wl.y[l], non_blocking=True)
         first[0] = False
 
-    K = max(4, args.steps // 2)
-    for _ in range(3):
-        step()
-    torch.cuda.synchronize()
-    barrier(ws)
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(K):
-        step()
-    comp.wait_stream(s_out)
-    e1.record()
-    torch.cuda.synchronize()
-    ms = max_over_ranks(e0.elapsed_time(e1) / K, ws)
-    barrier(ws)
+    def timed(K, compute):
+        for _ in range(3):
+            step(compute)
+        torch.cuda.synchronize()
+        barrier(ws)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(K):
+            step(compute)
+        comp.wait_stream(s_out)
+        e1.record()
+        torch.cuda.synchronize()
+        wall = (time.perf_counter() - t0) * 1e3 / K
+        ms = max_over_ranks(e0.elapsed_time(e1) / K, ws)
+        barrier(ws)
+        return ms, wall
+
+    K = e2e_steps(args)
+    ms, wall = timed(K, True)
+    ms_copy, _ = timed(K, False)
     return {"value": round(ws * B / (ms / 1e3), 1), "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),
-            "d2h_bytes_per_step": int(d2h), "ms_per_step": round(ms, 3),
-            "wall_ms_per_step": round((time.perf_counter() - t0) * 1e3 / K, 3)}
+            "d2h_bytes_per_step": int(d2h), "ms_per_step": round(ms, 3), "steps": K,
+            "wall_ms_per_step": round(wall, 3),
+            "copy_only": {"ms_per_step": round(ms_copy, 3),
+                          "gbs_per_gpu": round((h2d + d2h) / (ms_copy / 1e3) / 1e9, 1),
+                          "tokens_per_s_ceiling": round(ws * B / (ms_copy / 1e3), 1),
+                          "note": "the same host copies with no compute, every rank at once"},
+            "bound": "host copies" if ms_copy >= 0.9 * ms else "device compute",
+            "pinned_numa_cpus": (f"{numa_cpus[0]}-{numa_cpus[-1]}" if numa_cpus else None)}
 
 
 def ragged_schedule(steps: int, rows: int, slots: int, seed: int, finish_p: float = 1.0 / 512,
-                    admit_p: float = 1.0 / 8, lo: int = 384, init: int = 416):
+                    admit_p: float = 1.0 / 8, lo: int = 384, init: int = 416, shards: int = 1):
     """Seeded continuous-batching admission process (host side, numpy).
 
     A batch of `rows` positions holds live sequences (a pool slot each) or padding (-1).
     Every step each live sequence finishes with probability `finish_p` (its slot returns
     to the free list) and each empty position admits a new sequence with probability
     `admit_p`, or always while fewer than `lo` are live.  Returns the per-step slot map
-    [steps, rows] and, per step, the slots admitted just before it (fresh state)."""
+    [steps, rows] and, per step, the slots admitted just before it (fresh state).
+
+    ``shards`` > 1: one global slot space over several GPUs.  Rows and slots split into
+    ``shards`` equal contiguous parts (slot shards as ``sharding.slot_range``); a row of part r
+    admits only slots of shard r, i.e. a new sequence is routed to a GPU with a free slot and
+    stays there; ``lo`` / ``init`` apply per part."""
     import numpy as np
-    if slots <= rows or not 0 < lo <= init <= rows:
-        raise ValueError(f"ragged schedule needs slots > rows >= init >= lo > 0 "
-                         f"(slots {slots}, rows {rows}, init {init}, lo {lo})")
+    if rows % shards or slots % shards:
+        raise ValueError(f"rows {rows} and slots {slots} must split into {shards} shards")
+    rs, ss = rows // shards, slots // shards
+    if ss <= rs or not 0 < lo <= init <= rs:
+        raise ValueError(f"ragged schedule needs slots > rows >= init >= lo > 0 per shard "
+                         f"(slots {ss}, rows {rs}, init {init}, lo {lo})")
     rng = np.random.default_rng(seed)
-    free = list(rng.permutation(slots))
+    free = [list(q * ss + rng.permutation(ss)) for q in range(shards)]
     cur = np.full(rows, -1, dtype=np.int32)
-    for r in rng.choice(rows, init, replace=False):
-        cur[r] = free.pop()
+    for q in range(shards):
+        for r in rng.choice(rs, init, replace=False):
+            cur[q * rs + r] = free[q].pop()
     initial = cur[cur >= 0].copy()
     sched = np.empty((steps, rows), dtype=np.int32)
     admits = []
@@ -568,16 +638,20 @@ def ragged_schedule(steps: int, rows: int, slots: int, seed: int, finish_p: floa
         new = []
         if k > 0:
             done = (cur >= 0) & (rng.random(rows) < finish_p)
-            free.extend(int(s) for s in cur[done])
+            for r in np.flatnonzero(done):
+                free[r // rs].append(int(cur[r]))
             cur[done] = -1
-            empty = np.flatnonzero(cur < 0)
-            take = empty[rng.random(empty.size) < admit_p]
-            need = lo - int((cur >= 0).sum())
-            if need > take.size:
-                take = np.union1d(take, empty[:need])
-            for r in take:
-                cur[r] = free.pop(0)
-                new.append(int(cur[r]))
+            admit_draw = rng.random(rows)
+            for q in range(shards):
+                part = cur[q * rs:(q + 1) * rs]
+                empty = np.flatnonzero(part < 0)
+                take = empty[admit_draw[q * rs:(q + 1) * rs][empty] < admit_p]
+                need = lo - int((part >= 0).sum())
+                if need > take.size:
+                    take = np.union1d(take, empty[:need])
+                for r in take:
+                    part[r] = free[q].pop(0)
+                    new.append(int(part[r]))
         sched[k] = cur
         admits.append(np.array(new, dtype=np.int32))
     return initial, sched, admits
@@ -591,11 +665,23 @@ def time_ragged(args, rank: int, ws: int):
     27-layer step is a CUDA graph reading the step's slot map from a device buffer;
     admissions (prefill split of a fresh N(0, 0.1) state into every layer) run between
     steps, outside the timed events.  tokens/s counts live rows only."""
+    import numpy as np
     from nested_ssm_b200 import TieredSlotPool, prefill_split, rot_flat, tiered_state_update
+    from nested_ssm_b200 import sharding as SH
     dev = torch.device("cuda")
     L, Bm, S, c, K = args.layers, args.batch, args.ragged_slots, args.chunk, args.ragged_steps
     W = max(3, args.warmup)
-    initial, sched, admits = ragged_schedule(W + K, Bm, S, seed=3000 + rank)
+    # one global schedule (same seed on every rank) over ws*Bm rows and ws*S slots; this rank
+    # serves its part of the rows, whose slots all lie in its shard, as local slot ids
+    g_initial, g_sched, g_admits = ragged_schedule(W + K, ws * Bm, ws * S, seed=3000, shards=ws)
+    lo_s, hi_s = SH.slot_range(ws * S, rank, ws)
+    part = g_sched[:, rank * Bm:(rank + 1) * Bm]
+    own = SH.owner_of(torch.from_numpy(part[part >= 0]), ws * S, ws)
+    assert bool((own == rank).all()), "a row was routed to a GPU that does not own its slot"
+    sched = np.where(part >= 0, part - lo_s, -1).astype(np.int32)
+    mine = lambda a: (a[(a >= lo_s) & (a < hi_s)] - lo_s).astype(np.int32)   # noqa: E731
+    initial = mine(g_initial)
+    admits = [mine(a) for a in g_admits]
     gen = torch.Generator(device=dev)
     gen.manual_seed(3000 + rank)
     pool = TieredSlotPool(L, S, H, P, N, G, args.hot, c, args.cold, torch.bfloat16, dev, max_batch=Bm)
@@ -681,11 +767,166 @@ def time_ragged(args, rank: int, ws: int):
             "warmup": W, "live_rows_per_step": round(live / K, 1), "padded_batch": Bm, "slots_per_gpu": S,
             "layers": L, "chunk": c, "n_gpus": ws, "admitted": int(sum(a.size for a in admits[W:])),
             "flush_phase_histogram_last_step": [int(v) for v in ph.tolist()],
+            "global_slots": ws * S,
             "config": "continuous batching: finish p=1/512, admit p=1/8 per empty row, >=384 live, "
-                      "padded to 448 with slot -1, per-slot flush phases; pool of %d slots x %d layers "
-                      "(%.1f GB; the configuration's 4096 slots x 27 layers exceed HBM)"
-                      % (S, L, L * S * bytes_per_slot(args) / 1e9),
+                      "padded to 448 with slot -1, per-slot flush phases; one global slot space of %d slots "
+                      "sharded by slot over %d GPU(s), %d slots x %d layers per GPU (%.1f GB; the "
+                      "configuration's 4096 slots x 27 layers per GPU exceed HBM)"
+                      % (ws * S, ws, S, L, L * S * bytes_per_slot(args) / 1e9),
             "gpu_launches_per_step": L * 3}
+
+
+def graph_of_steps(wl: Workload, k0: int):
+    """CUDA graph of Workload.NI consecutive steps starting at input set k0."""
+    cap = torch.cuda.Stream()
+    cap.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(cap):
+        with torch.cuda.graph(g, stream=cap):
+            for k in range(Workload.NI):
+                wl.step(k0 + k)
+    torch.cuda.current_stream().wait_stream(cap)
+    torch.cuda.synchronize()
+    return g
+
+
+# The reference's own measurement of this configuration (scale/bench_v4_decode.json: B=256,
+# pb=32, c=4, its fp8-cold arm), ms per 27-layer step.
+REF_CONFIG1_FP8_MS = 39.0069
+
+
+def time_config1(args, rank: int, ws: int):
+    """B=256 sequences per GPU, 27 layers, c=4, fp8 cold, 256 decode steps
+    timed (64 replays of a 4-step CUDA graph: whole c-cycles), inputs resident in HBM."""
+    a = argparse.Namespace(**vars(args))
+    a.batch, a.chunk, a.cold, a.hot = 256, 4, "fp8", 32
+    wl = Workload(a, rank)
+    for k in range(3):
+        wl.step(k)
+    g = graph_of_steps(wl, 3)
+    g.replay()
+    reps = 256 // Workload.NI
+    barrier(ws)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / (reps * Workload.NI), ws)
+    barrier(ws)
+    wl.pool.check_status()
+    del g, wl
+    torch.cuda.empty_cache()
+    return {"batch_per_gpu": 256, "layers": 27, "chunk": 4, "cold": "fp8", "steps": reps * Workload.NI,
+            "tokens_per_s": round(ws * 256 / (ms / 1e3), 1), "ms_per_step": round(ms, 4),
+            "reference_published_ms_per_step": REF_CONFIG1_FP8_MS,
+            "speedup_vs_reference_published": round(REF_CONFIG1_FP8_MS / ms, 2)}
+
+
+REF_DIR = os.path.join(REPO, "baseline", "_ref")
+
+
+def reference_gpu_leg(batches=(448, 256), pb: int = 32, c: int = 4):
+    """The reference's own GPU decode arms, unmodified (``run_point`` of its
+    scale/bench_v4_decode.py, installed into baseline/_ref by baseline/install.sh): fla's
+    fused recurrent kernel as the fresh op, its v4 arms with fp32 / bf16 / fp8 cold (the fp8
+    arm with its own Triton dequant-matvec); the SSU arms need mamba_ssm, absent here.  Runs
+    in this process; bench.py starts it in a fresh interpreter."""
+    if not os.path.exists(os.path.join(REF_DIR, "bench_v4_decode.py")):
+        return {"unavailable": "baseline/_ref/bench_v4_decode.py is not installed (baseline/install.sh)"}
+    sys.path.insert(0, REF_DIR)
+    import bench_v4_decode as RB   # noqa: E402  (the reference module, unmodified)
+    out = {"source": "reference scale/bench_v4_decode.py run_point (unmodified), same box", "points": []}
+    for b in batches:
+        r = RB.run_point(b, pb, c, "cuda")
+        keep = {k: (round(v, 4) if isinstance(v, float) and math.isfinite(v) else None)
+                for k, v in r.items() if k.endswith(("_ms", "_toks")) or k in ("B", "pb", "c")}
+        out["points"].append(keep)
+        torch.cuda.empty_cache()
+    return out
+
+
+def reference_gpu_leg_isolated(args):
+    cmd = [sys.executable, os.path.abspath(__file__), "--reference-gpu-leg-only"]
+    env = dict(os.environ)
+    for k in ("RANK", "LOCAL_RANK", "WORLD_SIZE", "MASTER_ADDR", "MASTER_PORT"):
+        env.pop(k, None)
+    try:
+        out = subprocess.run(cmd, capture_output=True, text=True, timeout=1200, env=env)
+        return json.loads(out.stdout.strip().splitlines()[-1])
+    except (subprocess.TimeoutExpired, ValueError, IndexError) as e:
+        return {"unavailable": f"reference GPU leg failed: {type(e).__name__}"}
+
+
+def multi_gpu_check(args, rank: int, ws: int):
+    """Slot-sharded correctness on hardware, outside the timed region: one global slot space
+    of ws*64 slots partitioned by slot (sharding.slot_range), a global batch of ws*48 rows with
+    a permuted slot map and padded rows.  Every rank serves the rows whose slots it owns
+    (sharding.local_batch) for 6 tokens (one flush at c=4; rotation by R on its GPU), y of
+    every token is gathered over NCCL (sharding.gather_rows), and rank 0 compares it with its
+    own GPU serving the whole global batch alone: the two must be bit-identical."""
+    from nested_ssm_b200 import TieredSlotPool, prefill_split, tiered_state_update
+    from nested_ssm_b200 import sharding as SH
+    dev = torch.device("cuda")
+    Sg, Bg, steps, c = 64 * ws, 48 * ws, 6, 4
+    gen = torch.Generator().manual_seed(4242)
+    slots_g = torch.randperm(Sg, generator=gen)[:Bg].to(torch.int32)
+    slots_g[torch.rand(Bg, generator=gen) < 0.05] = -1
+    A = -torch.exp(torch.rand(H, generator=gen) * math.log(16.0))
+    D = torch.randn(H, generator=gen)
+    dtb = torch.log(torch.expm1(torch.rand(H, generator=gen) * (0.1 - 1e-3) + 1e-3))
+    R = torch.linalg.qr(torch.randn(G, N, N, generator=gen))[0].contiguous()
+    xs = torch.randn(steps, Bg, H, P, generator=gen).to(torch.bfloat16)
+    dts = torch.randn(steps, Bg, H, generator=gen).to(torch.bfloat16)
+    Bs = (torch.randn(steps, Bg, G, N, generator=gen) / math.sqrt(N)).to(torch.bfloat16)
+    Cs = (torch.randn(steps, Bg, G, N, generator=gen) / math.sqrt(N)).to(torch.bfloat16)
+    A, D, dtb, R = A.to(dev), D.to(dev), dtb.to(dev), R.to(dev)
+
+    def fill(pool, lo, hi):
+        """Prefill global slots [lo, hi) into pool slots 0.. from one seeded global stream."""
+        g = torch.Generator(device=dev).manual_seed(99)
+        for s0 in range(0, Sg, 64):
+            st = torch.randn(64, H, P, N, device=dev, generator=g) * math.sqrt(0.1)
+            sel = [i for i in range(64) if lo <= s0 + i < hi]
+            if sel:
+                loc = torch.tensor([s0 + i - lo for i in sel], dtype=torch.int32, device=dev)
+                prefill_split(pool, 0, st[sel].contiguous(), loc)
+
+    lo, hi = SH.slot_range(Sg, rank, ws)
+    pool = TieredSlotPool(1, hi - lo, H, P, N, G, args.hot, c, args.cold, torch.bfloat16, dev, max_batch=Bg)
+    fill(pool, lo, hi)
+    rows, lsl = SH.local_batch(slots_g, rank, ws, Sg)
+    gathered = []
+    for k in range(steps):
+        y = torch.zeros(rows.numel(), H, P, dtype=torch.bfloat16, device=dev)
+        if rows.numel():
+            tiered_state_update(pool, 0, xs[k][rows].to(dev), dts[k][rows].to(dev), A, Bs[k][rows].to(dev),
+                                Cs[k][rows].to(dev), D, dtb, True, lsl.to(dev), -1, y, R, 1e-3)
+        gathered.append(SH.gather_rows(y, rows.to(dev), Bg))
+    torch.cuda.synchronize()
+    pool.check_status()
+    n_rows = int(rows.numel())
+    del pool
+    if rank != 0:
+        return None
+    single = TieredSlotPool(1, Sg, H, P, N, G, args.hot, c, args.cold, torch.bfloat16, dev, max_batch=Bg)
+    fill(single, 0, Sg)
+    worst, equal = 0.0, True
+    for k in range(steps):
+        y1 = torch.zeros(Bg, H, P, dtype=torch.bfloat16, device=dev)
+        tiered_state_update(single, 0, xs[k].to(dev), dts[k].to(dev), A, Bs[k].to(dev), Cs[k].to(dev), D, dtb,
+                            True, slots_g.to(dev), -1, y1, R, 1e-3)
+        equal &= bool(torch.equal(y1, gathered[k]))
+        worst = max(worst, float((y1.float() - gathered[k].float()).abs().max()))
+    single.check_status()
+    del single
+    torch.cuda.empty_cache()
+    return {"pass": equal, "max_abs_diff": worst, "global_slots": Sg, "global_batch": Bg,
+            "padded_rows": int((slots_g < 0).sum()), "rows_on_rank0": n_rows, "steps": steps,
+            "check": "y of every token, slot-sharded over the ranks and gathered over NCCL, "
+                     "bit-identical to one GPU serving the whole global batch"}
 
 
 # --------------------------------------------------------------------------
@@ -792,6 +1033,9 @@ def main():
     if args.cpu_leg_only:
         print(json.dumps(cpu_baseline_leg(args)), flush=True)
         return 0
+    if args.reference_gpu_leg_only:
+        print(json.dumps(reference_gpu_leg()), flush=True)
+        return 0
     rank, ws, local = dist_init()
     if not torch.cuda.is_available():
         raise SystemExit("bench.py needs a CUDA device")
@@ -891,7 +1135,7 @@ def main():
                                       for i in range(len(kd_all) // L)],
                 "step_gbs_incl_rotation": round(L * B * bps / (ms / 1e3) / 1e9, 1)}
 
-    e2e = None if args.no_e2e else time_e2e(wl, args, ws)
+    e2e = None if args.no_e2e else time_e2e(wl, args, ws, local)
     del wl
     torch.cuda.empty_cache()
     fresh = None if args.no_fresh else time_fresh(args, rank, ws)
@@ -899,16 +1143,33 @@ def main():
     prefill = None if args.no_prefill else time_prefill(args, rank, ws)
     torch.cuda.empty_cache()
     ragged = None if args.no_ragged else time_ragged(args, rank, ws)
+    torch.cuda.empty_cache()
+    config1 = None if args.no_config1 else time_config1(args, rank, ws)
+    mcheck = None if (ws == 1 or args.no_multi_gpu_check) else multi_gpu_check(args, rank, ws)
+    ref_gpu = None
+    if rank == 0 and ws == 1 and not args.no_reference_gpu:
+        torch.cuda.empty_cache()
+        ref_gpu = reference_gpu_leg_isolated(args)
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu:
         cpu = cpu_baseline_leg_isolated(args)
 
     if rank == 0:
+        # vs_baseline: against the reference's own fp8-cold arm measured on this box in this run
+        # when that leg ran, else against its published number (other box)
+        ref_same = None
+        if ref_gpu and ref_gpu.get("points"):
+            ref_same = next((p_.get("v4fp8_toks") for p_ in ref_gpu["points"] if p_.get("B") == B), None)
+        base_toks = ref_same if ref_same else REF_PUBLISHED_TOKS
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": ws, "steps": K,
             "warmup": W, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": round(value / (ws * REF_PUBLISHED_TOKS), 3),
+            "vs_baseline": round(value / (ws * base_toks), 3),
+            "vs_baseline_denominator": ("reference fp8-cold arm, same box, this run (tokens/s per GPU): %.1f"
+                                        % ref_same) if ref_same else
+                                       ("reference published fp8-cold arm (other box): %.1f tokens/s"
+                                        % REF_PUBLISHED_TOKS),
             "dtype": f"{args.cold}-cold/fp32-hot (bf16 io)", "data": "synthetic",
             "config": {"workload": f"tiered c={args.chunk} {args.cold}-cold hot={args.hot}, B={B}/GPU, "
                                    f"{L} layers, H={H} P={P} N={N} G={G}",
@@ -925,6 +1186,9 @@ def main():
             "conv_step": conv,
             "prefill_scan": prefill,
             "ragged": ragged,
+            "config1": config1,
+            "reference_gpu": ref_gpu,
+            "multi_gpu_check": mcheck,
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)

@@ -294,6 +294,24 @@ NSSM_API int nssm_rot_flat(const void* x, int64_t x_stride, int32_t dtype, const
  * widths[0..n) (n <= cap); returns n. */
 NSSM_API int32_t nssm_supported_hot_dims(int32_t dstate, int32_t* widths, int32_t cap);
 
+/* Upper bound on the polls of every bounded wait inside the persistent decode kernels
+ * (nssm_tiered_step / nssm_tiered_step_static); 0 restores the default (2^26, seconds).
+ * A wait that runs out sets bit 1 of *status, lets the copies already issued land and
+ * returns without finishing its items (outputs and pool rows of that call are then
+ * undefined).  Process-wide; read at each launch.  For failure-detection tests and
+ * callers that want a shorter watchdog.  Returns the previous value.  No counterpart in
+ * the reference (its torch ops have no device-side waits). */
+NSSM_API uint32_t nssm_set_wait_polls(uint32_t polls);
+
+/* Failure injection for tests of the timeout path; never enable it in production.  While
+ * enabled, every persistent STEP launch makes its first CTA announce 16 bytes more than
+ * the copies of its first item deliver, so that item's pipeline wait can never complete:
+ * the CTA's waits run out after the nssm_set_wait_polls limit, bit 1 of *status is set and
+ * the call returns (that call's outputs and pool rows are undefined).  No device fault,
+ * trap or unbounded wait is involved.  Returns the previous setting.  No counterpart in
+ * the reference. */
+NSSM_API int32_t nssm_test_inject_stuck_copy(int32_t enable);
+
 /* sizeof of the argument structs, for binding checks. */
 NSSM_API size_t nssm_sizeof_pool(void);
 NSSM_API size_t nssm_sizeof_step_args(void);

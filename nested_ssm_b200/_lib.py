@@ -22,7 +22,7 @@ EXPORTED = (
     "nssm_materialize", "nssm_rot_flat", "nssm_supported_hot_dims", "nssm_sizeof_pool",
     "nssm_sizeof_step_args", "nssm_abi_version", "nssm_last_error", "nssm_tiered_step_static",
     "nssm_conv_step", "nssm_sizeof_conv_args", "nssm_gated_rmsnorm", "nssm_chunk_scan",
-    "nssm_sizeof_scan_args",
+    "nssm_sizeof_scan_args", "nssm_set_wait_polls", "nssm_test_inject_stuck_copy",
 )
 
 
@@ -139,6 +139,8 @@ def load(auto_build: bool = True) -> C.CDLL:
             "nssm_sizeof_step_args": (sz, []),
             "nssm_abi_version": (i32, []),
             "nssm_last_error": (C.c_char_p, []),
+            "nssm_set_wait_polls": (C.c_uint32, [C.c_uint32]),
+            "nssm_test_inject_stuck_copy": (i32, [i32]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(lib, name)

@@ -72,6 +72,14 @@ int smem_optin(int* out) {
   return NSSM_OK;
 }
 
+std::atomic<uint32_t> g_wait_polls{nssm::kSpinLimit};
+
+uint32_t wait_polls() { return g_wait_polls.load(std::memory_order_relaxed); }
+
+std::atomic<int> g_inject_stuck{0};
+
+int inject_stuck() { return g_inject_stuck.load(std::memory_order_relaxed); }
+
 int sm_count(int* out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return cuda_check("cudaGetDevice");
@@ -406,6 +414,14 @@ int32_t nssm_supported_hot_dims(int32_t dstate, int32_t* widths, int32_t cap) {
     ++n;
   }
   return n;
+}
+
+uint32_t nssm_set_wait_polls(uint32_t polls) {
+  return g_wait_polls.exchange(polls ? polls : nssm::kSpinLimit, std::memory_order_relaxed);
+}
+
+int32_t nssm_test_inject_stuck_copy(int32_t enable) {
+  return g_inject_stuck.exchange(enable ? 1 : 0, std::memory_order_relaxed);
 }
 
 size_t nssm_sizeof_pool(void) { return sizeof(nssm_pool); }

@@ -22,6 +22,8 @@ int cuda_check(const char* what);
 int occupancy(const void* fn, int smem, int threads, int* occ_out);
 int sm_count(int* out);
 int smem_optin(int* out);
+uint32_t wait_polls();   // polls of a bounded pipeline wait (nssm_set_wait_polls)
+int inject_stuck();      // failure injection for tests (nssm_test_inject_stuck_copy)
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
@@ -73,6 +75,8 @@ inline int launch_phase(const nssm::StepParams& sp, int batch, cudaStream_t st, 
     pp.sp = sp;
     pp.items = (int)items;
     pp.ring_in_stage = ring_ok ? 1 : 0;
+    pp.polls = wait_polls();
+    pp.inject_stuck = PHASE == nssm::PH_STEP ? inject_stuck() : 0;
     // deepest pipeline (up to the phase's stage count) whose CTAs fit `target` per SM
     int nst = nssm::stages_for(PHASE);
     for (; nst >= 2; --nst) {

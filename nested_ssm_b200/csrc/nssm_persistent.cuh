@@ -53,7 +53,7 @@ constexpr int kPW = kPT / 32;              // warps per CTA
 constexpr int kPMaxPersistent = 80;        // headdim bound of the persistent path (10 rows per warp)
 constexpr int kRingInStage = 16;           // c up to this: the ring rides in the stage
 constexpr int kRingF32Max = 8;             // c up to this: each warp keeps the ring B as fp32
-constexpr uint32_t kSpinLimit = 1u << 26;  // bounded mbarrier wait, then error + exit
+constexpr uint32_t kSpinLimit = 1u << 26;  // default polls of a bounded mbarrier wait, then error + exit
 enum : int { STATUS_TIMEOUT = 2 };
 enum : int { PH_STEP = 0, PH_FLUSH = 1 };
 
@@ -109,9 +109,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait; false on timeout.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
-  for (uint32_t it = 0; it < kSpinLimit; ++it)
+// Bounded wait of at most `polls` tries; false on timeout.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint32_t polls = kSpinLimit) {
+  for (uint32_t it = 0; it < polls; ++it)
     if (mbar_try_wait(bar, parity)) return true;
   return false;
 }
@@ -199,6 +199,8 @@ struct PParams {
   PLayout L;
   int items;          // batch * H
   int ring_in_stage;  // the ring rides in the stage (c <= kRingInStage, aligned)
+  uint32_t polls;     // polls of a pipeline wait before it gives up (kSpinLimit by default)
+  int inject_stuck;   // failure injection (tests only): CTA 0's first item never completes
 };
 
 __device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
@@ -475,8 +477,10 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
   const int h_beg = beg - b0 * H;
   const Cur start{b0, h_beg, h_beg / HG, h_beg % HG};
 
-  // ---- producer: bulk copies of item q into stage s (one thread)
-  auto issue = [&](const Cur& q, int s) {
+  // ---- producer: bulk copies of item q into stage s (one thread).  `stuck` (failure
+  // injection) announces 16 bytes more than the copies deliver, so that stage's phase
+  // never completes and its waits run out.
+  auto issue = [&](const Cur& q, int s, bool stuck = false) {
     const int j = q.b - b0, b = q.b, h = q.h, g = q.g;
     const int slot = bslot[j];
     const int64_t sh = (int64_t)slot * H + h;
@@ -485,7 +489,7 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
     if (COLD == COLD_FP8) bytes += Pn * 4;
     if (STEP) bytes += (uint32_t)(Pn * PB * 4 + Pn * IOB + 2 * N * IOB);
     if (ring_st) bytes += (uint32_t)(c * Pn * IOB + c * NC * 4 + cp * 4);
-    mbar_expect_tx(&full[s], bytes);
+    mbar_expect_tx(&full[s], bytes + (stuck ? 16u : 0u));
     bulk_g2s(st + L.s_cold, static_cast<const char*>(p.cold) + sh * Pn * NC * ESZ, Pn * NC * ESZ, &full[s]);
     if (COLD == COLD_FP8) bulk_g2s(st + L.s_scale, p.scale + sh * Pn, Pn * 4, &full[s]);
     if (STEP) {
@@ -508,9 +512,10 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
   Cur pq = start;
   first_valid(pq);
   uint32_t n_issued = 0;
+  const bool inject = STEP && pp.inject_stuck != 0 && blockIdx.x == 0;
   if (tid == 0) {
     for (int s = 0; s < kStages && pq.b * H + pq.h < end; ++s) {
-      issue(pq, s);
+      issue(pq, s, inject && s == 0);
       ++n_issued;
       advance(pq);
     }
@@ -542,7 +547,9 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
     const int slot = bslot[j0b], tnew = btn[j0b];
     const int64_t sh = (int64_t)slot * H + h;
     const unsigned char* st = sm + s * L.stage_bytes;
-    if (!mbar_wait_bounded(&full[s], par)) { ok = false; break; }
+    // every lane waits on the stage's copies itself (acquire); the warp leaves together
+    // if any lane's wait ran out, so no lane reaches the warp-wide shuffles alone
+    if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full[s], par, pp.polls))) { ok = false; break; }
     const uint4* csm = reinterpret_cast<const uint4*>(st + L.s_cold);
     auto ring_x_at = [&](int j, int r) -> float {
       return ring_st ? ldv<IOBF>(st + L.s_rx, j * Pn + r) : ldv<IOBF>(p.ring_x, (sh * c + j) * Pn + r);
@@ -957,18 +964,24 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
     // ---- release a stage once this warp's bulk store has read it; the producer refills
     // it once every warp has.  STEP releases the stage it just used.  FLUSH releases the
     // previous item's stage, so the bulk store of a band overlaps the next item's work.
+    // The producer (thread 0) waits for the stage to empty; its verdict is broadcast to
+    // warp 0 so that the whole warp leaves together when that wait runs out.
     __syncwarp();
+    bool prod_fail = false;
     if constexpr (STEP) {
       if (lane == 0) {
         bulk_wait_read_all();
         mbar_arrive(&empty[s]);
       }
       if (tid == 0 && pq.b * H + pq.h < end) {
-        if (!mbar_wait_bounded(&empty[s], par)) { ok = false; break; }
-        fence_proxy_async_smem();
-        issue(pq, s);
-        ++n_issued;
-        advance(pq);
+        if (!mbar_wait_bounded(&empty[s], par, pp.polls)) {
+          prod_fail = true;
+        } else {
+          fence_proxy_async_smem();
+          issue(pq, s);
+          ++n_issued;
+          advance(pq);
+        }
       }
     } else {
       if (k > 0) {
@@ -977,28 +990,35 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
           mbar_arrive(&empty[s_prev]);
         }
         if (tid == 0 && pq.b * H + pq.h < end) {
-          if (!mbar_wait_bounded(&empty[s_prev], par_prev)) { ok = false; break; }
-          fence_proxy_async_smem();
-          issue(pq, s_prev);
-          ++n_issued;
-          advance(pq);
+          if (!mbar_wait_bounded(&empty[s_prev], par_prev, pp.polls)) {
+            prod_fail = true;
+          } else {
+            fence_proxy_async_smem();
+            issue(pq, s_prev);
+            ++n_issued;
+            advance(pq);
+          }
         }
       }
       s_prev = s;
       par_prev = par;
     }
+    if (warp == 0 && __shfl_sync(0xffffffffu, prod_fail, 0)) { ok = false; break; }
     if (++s == kStages) { s = 0; par ^= 1u; }
   }
   if (lane == 0) bulk_wait_all();   // this warp's bulk stores are complete before exit
-  if (!ok && tid == 0) {
-    // a wait timed out: flag it and keep the CTA (and its shared memory) alive until
-    // the copies it issued have landed (bounded again)
-    if (p.status) atomicOr(p.status, STATUS_TIMEOUT);
-    int sq = 0;
-    uint32_t pq2 = 0;
-    for (uint32_t qn = 0; qn < n_issued; ++qn) {
-      mbar_wait_bounded(&full[sq], pq2);
-      if (++sq == kStages) { sq = 0; pq2 ^= 1u; }
+  if (!ok) {
+    if (lane == 0 && p.status) atomicOr(p.status, STATUS_TIMEOUT);
+    if (tid == 0) {
+      // a wait ran out: keep the CTA (and its shared memory) alive until the copies it
+      // issued have landed.  Item n went to stage n % kStages as that stage's phase
+      // n / kStages; only the last kStages items can still be in flight, and each is the
+      // latest phase of its stage, so its parity identifies it (bounded again, with the
+      // default poll count; the injected stuck phase, whose copies have all landed, with the
+      // caller's).
+      const uint32_t first = n_issued > (uint32_t)kStages ? n_issued - (uint32_t)kStages : 0u;
+      for (uint32_t qn = first; qn < n_issued; ++qn)
+        mbar_wait_bounded(&full[qn % kStages], (qn / kStages) & 1u, (inject && qn == 0) ? pp.polls : kSpinLimit);
     }
   }
 }

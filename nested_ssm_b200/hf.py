@@ -47,6 +47,31 @@ def _rotation_and_act(mixer):
     return None
 
 
+def _width_mask(mixer, rows: int, device) -> torch.Tensor | None:
+    """Mask of the rotated B / C coordinates the mixer's ActRotMask keeps, or None when it
+    keeps all of them.  ``ActRotMask._mask`` (scale/nemotron_retrofit.py:29-37) zeroes the
+    coordinates ``n >= width`` of every group after the rotation; an int width applies to every
+    row, a 1-D tensor width holds one width per batch row (it broadcasts against the batch
+    axis).  The width is read at every call, so ``set_width`` (nemotron_retrofit.py:112-114)
+    takes effect on the next token.  Returns a float mask that broadcasts against
+    ``[rows, G, N]``."""
+    act = mixer.act
+    if not (hasattr(act, "R") and hasattr(act, "width")):
+        return None
+    N = mixer.ssm_state_size
+    w = act.width
+    idx = torch.arange(N, device=device)
+    if torch.is_tensor(w) and w.dim() > 0:
+        w = w.reshape(-1).to(device)
+        if w.numel() != rows:
+            raise ValueError(f"ActRotMask width holds {w.numel()} per-row widths for a batch of {rows}")
+        return (idx[None, :] < w[:, None]).float()[:, None, :]
+    w = int(w)
+    if w >= N:
+        return None
+    return (idx < w).float()[None, None, :]
+
+
 def _decode(self, input_states, cache_params):
     """One decode token: _v4_decode (scale/v4_native_decode.py:29-172) on the GPU kernels."""
     st = self._nssm
@@ -63,6 +88,10 @@ def _decode(self, input_states, cache_params):
     x, Bv, Cv = conv_step(xbc[:, 0].contiguous(), conv_state, self.conv1d.weight,
                           self.conv1d.bias if self.use_conv_bias else None, "silu", None, -1, st["R"],
                           nheads=H, headdim=P, ngroups=G, dstate=N)
+    mask = _width_mask(self, b, Bv.device)
+    if mask is not None:   # ActRotMask's width mask on the rotated B and C
+        Bv = Bv * mask.to(Bv.dtype)
+        Cv = Cv * mask.to(Cv.dtype)
     A = -torch.exp(self.A_log.float())
     y = torch.empty(b, H, P, dtype=dtype, device=input_states.device)
     tiered_state_update(st["pool"], 0, x, dt[:, 0], A, Bv, Cv, self.D, self.dt_bias, True, st["slots"], -1, y,
@@ -106,7 +135,13 @@ def _lean_prefill(self, input_states, cache_params, attention_mask):
     xbc_t = xbc.transpose(1, 2)
     if cache_params is not None:
         cache_params.update_conv_state(F.pad(xbc_t, (self.conv_kernel_size - xbc_t.shape[-1], 0)), self.layer_idx)
-    conv = F.silu(self.conv1d(xbc_t)[..., :T].float()).to(dtype).transpose(1, 2).contiguous()   # [b, T, conv_dim]
+    # conv + bias + SiLU in fp32, rounded once to the activation dtype (causal_conv1d_fn's
+    # rounding, scale/v4_native_decode.py:198-200)
+    K = self.conv_kernel_size
+    w = self.conv1d.weight.float()
+    bias = self.conv1d.bias.float() if self.conv1d.bias is not None else None
+    conv = F.conv1d(xbc_t.float(), w, bias, padding=K - 1, groups=w.shape[0])[..., :T]
+    conv = F.silu(conv).to(dtype).transpose(1, 2).contiguous()   # [b, T, conv_dim]
     x = conv[..., :I].view(b, T, H, P)
     Bm, Cm = conv[..., I:I + GN], conv[..., I + GN:]
     if st["R"] is not None:
@@ -114,6 +149,10 @@ def _lean_prefill(self, input_states, cache_params, attention_mask):
             st["R"] = st["R"].to(conv.device, torch.float32).contiguous()
         Bm = rot_flat(Bm.reshape(b * T, GN), st["R"])
         Cm = rot_flat(Cm.reshape(b * T, GN), st["R"])
+    mask = _width_mask(self, b, conv.device)
+    if mask is not None:   # ActRotMask's width mask, per row over every prompt token
+        Bm = (Bm.reshape(b, T, G, N) * mask[:, None].to(Bm.dtype)).reshape(b * T, GN)
+        Cm = (Cm.reshape(b, T, G, N) * mask[:, None].to(Cm.dtype)).reshape(b * T, GN)
     A = -torch.exp(self.A_log.float())
     lim = getattr(self, "time_step_limit", None)
     lim = (0.0, math.inf) if lim is None else (float(lim[0]), float(lim[1]))

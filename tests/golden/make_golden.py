@@ -38,6 +38,11 @@ regenerate (checksums stored beside the outputs):
   reference's ``ActRotMask`` with seeded rotations, ``install(model, pb=32, c=4,
   cold_bf16=0)`` (``scale/v4_native_decode.py:247-256``, the HF torch prefill), then greedy
   ``generate``: the tokens and the logits of every step.
+* ``hf_generate_width.npz`` -- the same model and prompt with the state term made dominant
+  (``hf_state_dominant``) and the rotated B and C masked to their first 64 coordinates
+  (``set_width(model, 64)``, ``scale/nemotron_retrofit.py:112-114``; ``ActRotMask._mask``
+  zeroes the coordinates at and past the width).  Both HF fixtures also hold every mixer's
+  output at every decode step.
 """
 from __future__ import annotations
 
@@ -62,6 +67,7 @@ VLLM = dict(b=2, S=4, H=8, P=80, N=128, G=2, pb=32, c=4, seed=12, steps=9, slots
 ROT = dict(T=6, G=2, N=128, seed=13)
 CONV = dict(b=2, H=16, P=80, N=128, G=2, pb=32, c=4, seed=14, steps=9, K=4)
 HF = dict(b=2, prompt=7, new=9, seed=15, pb=32, c=4)
+HF_WIDTH = 64
 PREFILL = dict(b=2, T=100, H=4, P=80, N=128, G=2, chunk=128, seed=16)
 
 
@@ -73,6 +79,17 @@ def hf_model(seed: int):
                           num_attention_heads=4, num_key_value_heads=2, head_dim=16)
     torch.manual_seed(seed)
     return NemotronHForCausalLM(cfg).float().eval()
+
+
+def hf_state_dominant(model):
+    """Make the state term dominate the mixers' output (D = 0, dt = softplus(dt_raw + 1)): in
+    the randomly initialised model the D x skip and the small initial dt leave the state op's
+    share of the mixer output near 1e-5, too little for a fixture to tell masks apart."""
+    for m in model.modules():
+        if type(m).__name__ == "NemotronHMamba2Mixer":
+            m.D.data.zero_()
+            m.dt_bias.data.fill_(1.0)
+    return model
 
 
 def hf_rotations(model, seed: int):
@@ -344,26 +361,44 @@ def make_prefill(ref):
     return out
 
 
-def make_hf(ref):
+def make_hf(ref, width=None):
     sys.path.insert(0, os.path.join(ref, "scale"))
     import v4_native_decode as V
     import nemotron_retrofit as NR
     cfg = HF
     model = hf_model(cfg["seed"])
+    if width is not None:
+        hf_state_dominant(model)
     Rs = hf_rotations(model, cfg["seed"])
     mixers = [m for m in model.modules() if type(m).__name__ == "NemotronHMamba2Mixer"]
     for m, R in zip(mixers, Rs):
         act = NR.ActRotMask(m.act, m.intermediate_size, m.n_groups, m.ssm_state_size)
         act.R.data.copy_(R)
         m.act = act
+    if width is not None:
+        NR.set_width(model, width)
     V.install(model, pb=cfg["pb"], c=cfg["c"], cold_bf16=0)
     for m in mixers:
         m.v4cfg["lean_prefill"] = 0          # the HF torch prefill (no fused kernels on CPU)
     g = torch.Generator().manual_seed(cfg["seed"] + 2)
     ids = torch.randint(0, 100, (cfg["b"], cfg["prompt"]), generator=g)
+    outs = mixer_decode_outputs(mixers)
     out = model.generate(ids, max_new_tokens=cfg["new"], do_sample=False, output_logits=True,
                          return_dict_in_generate=True)
-    return dict(ids=ids, tokens=out.sequences, logits=torch.stack(out.logits).float())
+    return dict(ids=ids, tokens=out.sequences, logits=torch.stack(out.logits).float(),
+                mixer_out=torch.stack([torch.stack(o) for o in outs]).float())
+
+
+def mixer_decode_outputs(mixers):
+    """Forward hooks recording every one-token call's output of each mixer (the decode steps):
+    the mixer output is far more sensitive to the state op than the logits of a random model."""
+    outs = [[] for _ in mixers]
+    for i, m in enumerate(mixers):
+        def hook(mod, args, out, i=i):
+            if out.shape[1] == 1:
+                outs[i].append(out.detach().clone())
+        m.register_forward_hook(hook)
+    return outs
 
 
 def save(name, arrays):
@@ -376,15 +411,23 @@ def save(name, arrays):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="checkout of omin-Kwon/nested_ssm")
+    ap.add_argument("--only", nargs="*", default=None, help="fixture file names to (re)make")
     a = ap.parse_args()
     torch.set_num_threads(max(1, os.cpu_count() or 1))
+    ref = a.reference
+    makers = {
+        "native_decode_fp32.npz": lambda: make_native(ref),
+        "vllm_fp8.npz": lambda: make_vllm(ref),
+        "rot_flat.npz": lambda: make_rot(ref),
+        "native_decode_conv.npz": lambda: make_native_conv(ref),
+        "hf_generate.npz": lambda: make_hf(ref),
+        "hf_generate_width.npz": lambda: make_hf(ref, width=HF_WIDTH),
+        "prefill_hf.npz": lambda: make_prefill(ref),
+    }
     with torch.no_grad():
-        save("native_decode_fp32.npz", make_native(a.reference))
-        save("vllm_fp8.npz", make_vllm(a.reference))
-        save("rot_flat.npz", make_rot(a.reference))
-        save("native_decode_conv.npz", make_native_conv(a.reference))
-        save("hf_generate.npz", make_hf(a.reference))
-        save("prefill_hf.npz", make_prefill(a.reference))
+        for name, make in makers.items():
+            if a.only is None or name in a.only:
+                save(name, make())
 
 
 if __name__ == "__main__":

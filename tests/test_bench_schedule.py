@@ -38,3 +38,24 @@ def test_ragged_schedule_invariants():
 def test_ragged_schedule_rejects_a_pool_no_larger_than_the_batch():
     with pytest.raises(ValueError, match="slots > rows"):
         bench.ragged_schedule(4, 448, 448, seed=0)
+
+
+def test_ragged_schedule_over_a_sharded_global_slot_space():
+    """ws GPUs share one global slot space: rows of part q (the q-th block of 448) only ever
+    hold slots of shard q (sharding.slot_range), every part keeps >= 384 live rows, and the
+    per-GPU view (local slot = global - first owned) is a valid single-GPU schedule."""
+    import torch
+    from nested_ssm_b200 import sharding as SH
+    ws, rows, slots, steps = 4, 448, 2048, 300
+    initial, sched, admits = bench.ragged_schedule(steps, ws * rows, ws * slots, seed=3000, shards=ws)
+    for q in range(ws):
+        lo, hi = SH.slot_range(ws * slots, q, ws)
+        part = sched[:, q * rows:(q + 1) * rows]
+        ids = part[part >= 0]
+        assert ids.min() >= lo and ids.max() < hi
+        assert bool((SH.owner_of(torch.from_numpy(ids), ws * slots, ws) == q).all())
+        assert (part >= 0).sum(axis=1).min() >= 384
+    for k in range(steps):
+        ids = sched[k][sched[k] >= 0]
+        assert len(set(ids.tolist())) == ids.size
+    assert sum(a.size for a in admits) > 0

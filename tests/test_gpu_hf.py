@@ -15,21 +15,33 @@ class RotAct(torch.nn.Module):
     reference's ActRotMask does for a full-width (unmasked) rotation
     (scale/nemotron_retrofit.py:18-54).  The decode path reads R and the SiLU from it."""
 
-    def __init__(self, act, inter, ngroups, dstate, R):
+    def __init__(self, act, inter, ngroups, dstate, R, width=None):
         super().__init__()
         self.act = act
         self.inter, self.ng, self.ds = inter, ngroups, dstate
         self.R = torch.nn.Parameter(R.clone())
+        self.width = dstate if width is None else width
 
     def forward(self, x):
         x = self.act(x)
         if x.dim() == 3 and x.shape[-1] == self.inter + 2 * self.ng * self.ds:
             h, B, C = torch.split(x, [self.inter, self.ng * self.ds, self.ng * self.ds], dim=-1)
             b, t, _ = B.shape
-            rot = lambda v: torch.einsum("btgn,gmn->btgm", v.view(b, t, self.ng, self.ds),  # noqa: E731
-                                         self.R.to(v.dtype)).reshape(b, t, -1)
+            keep = (torch.arange(self.ds, device=x.device) < self.width).to(x.dtype)   # int width
+            rot = lambda v: (torch.einsum("btgn,gmn->btgm", v.view(b, t, self.ng, self.ds),  # noqa: E731
+                                          self.R.to(v.dtype)) * keep).reshape(b, t, -1)
             x = torch.cat([h, rot(B), rot(C)], dim=-1)
         return x
+
+
+def _mixer_decode_outputs(mixers):
+    outs = [[] for _ in mixers]
+    for i, m in enumerate(mixers):
+        def hook(mod, args, out, i=i):
+            if out.shape[1] == 1:
+                outs[i].append(out.detach().float().cpu().clone())
+        m.register_forward_hook(hook)
+    return outs
 
 
 def test_hf_generate_matches_reference_install():
@@ -53,6 +65,37 @@ def test_hf_generate_matches_reference_install():
     assert torch.equal(out.sequences.cpu(), d["tokens"])
     for m in mixers:   # the decode went through the tiered pool
         assert m._nssm["pool"] is not None and int(m._nssm["pool"].t[0].max()) == cfg["new"] - 1
+
+
+def test_hf_width_mask_matches_reference():
+    """ActRotMask's width (the reference's set_width, scale/nemotron_retrofit.py:112-114) masks
+    the rotated B and C to their first 64 coordinates; hf_generate_width.npz holds the
+    reference's install + generate with that mask on a model whose mixer output is dominated
+    by the state term.  Every mixer's output at every decode step must match it to 2e-3 of its
+    magnitude (ignoring the mask moves it by ~95%)."""
+    from nested_ssm_b200.hf import install
+    d = GD.load("hf_generate_width.npz")
+    cfg = GD.MG.HF
+    torch.backends.cudnn.allow_tf32 = False
+    torch.backends.cuda.matmul.allow_tf32 = False
+    model = GD.MG.hf_state_dominant(GD.MG.hf_model(cfg["seed"]))
+    Rs = GD.MG.hf_rotations(model, cfg["seed"])
+    mixers = [m for m in model.modules() if type(m).__name__ == "NemotronHMamba2Mixer"]
+    for m, R in zip(mixers, Rs):
+        m.act = RotAct(m.act, m.intermediate_size, m.n_groups, m.ssm_state_size, R, width=GD.MG.HF_WIDTH)
+    model = model.cuda()
+    assert install(model, pb=cfg["pb"], c=cfg["c"], cold_bf16=0) == len(mixers)
+    outs = _mixer_decode_outputs(mixers)
+    with torch.no_grad():
+        out = model.generate(d["ids"].cuda(), max_new_tokens=cfg["new"], do_sample=False, output_logits=True,
+                             return_dict_in_generate=True)
+    got = torch.stack([torch.stack(o) for o in outs])
+    ref = d["mixer_out"]
+    assert got.shape == ref.shape
+    scale = float(ref.abs().max())
+    err = float((got - ref).abs().max())
+    assert err <= 2e-3 * scale, f"mixer outputs differ by {err:.3e} (|ref| max {scale:.3e})"
+    assert torch.equal(out.sequences.cpu(), d["tokens"])
 
 
 def _bf16_model(seed: int):

@@ -50,7 +50,8 @@ def test_static_scratch_matches_workspace_entry(io_dtype):
         ref, got = ys["nssm_tiered_step"], ys["nssm_tiered_step_static"]
         Hh.assert_y_close(got, ref.cpu(), f"step {step}")
         a, b = pools["nssm_tiered_step"], pools["nssm_tiered_step_static"]
-        torch.testing.assert_close(b.hot.cpu(), a.hot.cpu(), rtol=1e-5, atol=1e-6)
+        # the same kernels on the same inputs: the hot state is bit-identical
+        assert torch.equal(b.hot.cpu(), a.hot.cpu())
         assert int(Hh.fp8_ulp_dist(b.cold, a.cold).max()) <= 1
         torch.testing.assert_close(b.scale.cpu(), a.scale.cpu(), rtol=1e-5, atol=0)
         assert torch.equal(b.t.cpu(), a.t.cpu())

@@ -841,7 +841,7 @@ def reference_gpu_leg(batches=(448, 256), pb: int = 32, c: int = 4):
     out = {"source": "reference scale/bench_v4_decode.py run_point (unmodified), same box", "points": []}
     for b in batches:
         r = RB.run_point(b, pb, c, "cuda")
-        keep = {k: (round(v, 4) if isinstance(v, float) and math.isfinite(v) else None)
+        keep = {k: (int(v) if isinstance(v, int) else round(float(v), 4) if math.isfinite(float(v)) else None)
                 for k, v in r.items() if k.endswith(("_ms", "_toks")) or k in ("B", "pb", "c")}
         out["points"].append(keep)
         torch.cuda.empty_cache()

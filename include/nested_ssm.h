@@ -259,6 +259,9 @@ NSSM_API int nssm_tiered_step(const nssm_pool* pool, const nssm_step_args* args,
  *    NSSM_ERR_INVALID.  Without R no scratch is used and there is no limit.
  *  - The first call on each device looks the array up (a one-time set-up, on
  *    the current device); make that call before any stream capture begins.
+ *    The address is kept for the life of the process: after cudaDeviceReset on
+ *    a device (which unloads the library's device memory there) this entry
+ *    point must not be called on that device again.
  *  - All calls on one device share the array: two calls with R that may run
  *    at the same time (different streams, or different host threads) race and
  *    corrupt each other's B and C.  Issue them on one stream. */

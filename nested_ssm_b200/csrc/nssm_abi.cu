@@ -64,6 +64,27 @@ int occupancy(const void* fn, int smem, int threads, int* occ_out) {
   return NSSM_OK;
 }
 
+// Per-(kernel, device) record that the dynamic shared-memory opt-in was set.
+struct AttrEntry { const void* fn; int dev; };
+AttrEntry g_attr[64];
+std::atomic<int> g_nattr{0};
+
+int ensure_smem_attr(const void* fn) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return cuda_check("cudaGetDevice");
+  const int n = g_nattr.load(std::memory_order_acquire);
+  for (int i = 0; i < n && i < 64; ++i)
+    if (g_attr[i].fn == fn && g_attr[i].dev == dev) return NSSM_OK;
+  int optin = 0;
+  if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
+    return cuda_check("cudaDeviceGetAttribute(smem opt-in)");
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, optin) != cudaSuccess)
+    return cuda_check("cudaFuncSetAttribute(max dynamic shared memory)");
+  const int slot = g_nattr.fetch_add(1, std::memory_order_acq_rel);
+  if (slot < 64) g_attr[slot] = AttrEntry{fn, dev};
+  return NSSM_OK;
+}
+
 int smem_optin(int* out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return cuda_check("cudaGetDevice");

@@ -33,7 +33,9 @@ std::atomic<void*> g_scratch_ptr[kMaxDevices];
 std::mutex g_setup_mu;
 
 // Device address of g_step_scratch on the current device; looked up once per
-// device (the first call), then read from the cache.
+// device (the first call), then read from the cache.  The cache lives as long as the
+// process: a cudaDeviceReset unloads the array on that device and leaves the cached
+// address stale, so callers do not use this entry point on a device after resetting it.
 int scratch_on_current_device(void** out) {
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);

@@ -1,9 +1,9 @@
 """GPU parity at the benchmarked batch sizes (B = 256, 257, 448 rows; H=128, P=80, N=128, fp8
 cold, c=4) against the CPU oracle on a sample of rows.
 
-FLUSH counts and numbers the batch's flushing rows in passes of 256 threads; at B > 256 the
-second pass (and the running row number carried across passes) decides which CTA replays
-which row.  Rows are independent, so the oracle only has to follow a sample of them (rows 0,
+FLUSH counts and numbers the batch's flushing rows in passes of one CTA's threads (160 in the
+quad-row kernel at headdim 80, 256 in the banded one); past the first pass the running row
+number carried across passes decides which CTA replays which row.  Rows are independent, so the oracle only has to follow a sample of them (rows 0,
 1, 255, 256, 257, 300, 447 where they exist and 32 random ones): before every step the
 oracle's copy of those rows is re-synced from the GPU pool, the whole batch steps on the GPU,
 the sampled rows step in the oracle, and y and the sampled pool rows are compared at the
@@ -125,7 +125,7 @@ def test_benchmarked_batch_sampled_rows(b, phases):
         Hh.assert_y_close(yg[rows], yo, f"B={b} {phases} step {s}")
         assert torch.all(yg[pad] == 0), "padded rows must be left untouched"
         orc.compare(gpool)
-        # rows past 256 at a chunk boundary on this token: FLUSH's second counting pass ran
+        # rows past 256 at a chunk boundary on this token: FLUSH's later counting passes ran
         fl = (~pad) & ((t_before + 1) % C == 0)
         flushed_rows_seen += int(fl[256:].sum()) if b > 256 else 0
     if b > 256:
@@ -134,18 +134,20 @@ def test_benchmarked_batch_sampled_rows(b, phases):
 
 
 def test_bench_graph_replay_sampled_rows():
-    """One replay of the benchmark's 27-layer CUDA graph (4 tokens, one flush per slot) at
-    B=448 against the oracle on sampled rows of layers 0, 13 and 26, free-running over the 4
-    tokens from the state before the replay (y of the last token, hot state to fp32
-    reassociation, cold within one fp8 ulp per flush)."""
+    """One replay of the benchmark's 27-layer CUDA graph (4 tokens from a chunk start; the
+    4th flushes every slot) at B=448 against the oracle on sampled rows of layers 0, 13 and
+    26, free-running over the 4 tokens from the state before the replay.  The last token's y
+    is read before its flush, so it is held to the per-step y bar plus the rounding of the
+    benchmark's bf16 output (2^-8 relative); hot state to fp32 reassociation; the flushed cold codes within
+    one fp8 ulp (the GPU's and the CPU's softplus may differ by an fp32 ulp in dt between
+    syncs, which can move a code by one step) and rarely different at all."""
     import argparse
     import bench
     from nested_ssm_b200 import rot_flat
     args = argparse.Namespace(layers=27, batch=448, hot=PB, chunk=C, cold="fp8")
     wl = bench.Workload(args, rank=0)
     NI = bench.Workload.NI
-    wl.step(0)                      # one eager token, so the graph starts mid-chunk (t = 1)
-    torch.cuda.synchronize()
+    assert NI == C
     g = torch.cuda.CUDAGraph()
     cap = torch.cuda.Stream()
     cap.wait_stream(torch.cuda.current_stream())
@@ -176,8 +178,54 @@ def test_bench_graph_replay_sampled_rows():
     g.replay()
     torch.cuda.synchronize()
     for l in layers:
-        Hh.assert_y_close_quantized(wl.y[l][rows.cuda()].cpu(), yo[l], f"layer {l}")
+        o = orcs[l].pool
+        assert int(o.t[0]) == NI and float(o.glog.abs().max()) == 0.0   # every sampled slot flushed
+        # the benchmark's y is bf16: its rounding adds up to 2^-8 relative to the y bar
+        torch.testing.assert_close(wl.y[l][rows.cuda()].float().cpu(), yo[l], rtol=Hh.Y_RTOL + 2.0 ** -8,
+                                   atol=Hh.Y_ATOL, msg=lambda m: f"layer {l}: {m}")
         orcs[l].compare(wl.pool, l, per_step=False)
+        d = Hh.fp8_ulp_dist(wl.pool.cold[l][orcs[l].gslots.cuda()].cpu(), o.cold)
+        assert int(d.max()) <= 1 and float((d > 0).float().mean()) <= 1e-3, f"layer {l}: cold codes"
     wl.pool.check_status()
     del g, wl
     torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("c", [16, 64])
+def test_flush_with_full_random_ring(c):
+    """The c = 16 / 64 FLUSH (the rank-c update on the tensor cores) with every ring entry
+    random: the ring's x, dt and B' of all slots are filled with seeded values (B' bf16-exact,
+    as the step writes it), the rows sit one to three tokens before their chunk boundary
+    (staggered phases, some rows past their first chunk) and then step per token from
+    identical state, so each token a third of the 96 rows replays a whole random ring."""
+    from nested_ssm_b200 import TieredSlotPool, tiered_state_update
+    b, S = 96, 100
+    gen = torch.Generator().manual_seed(500 + c)
+    slot_of_row = torch.randperm(S, generator=gen)[:b]
+    gpool = TieredSlotPool(1, S, H, P, N, G, PB, c, "fp8", torch.bfloat16, "cuda", max_batch=b)
+    _prefill_random(gpool, S, seed=c)
+    g = torch.Generator(device="cuda").manual_seed(c)
+    gpool.ring_x[0].copy_(torch.randn(gpool.ring_x[0].shape, device="cuda", generator=g).to(torch.bfloat16))
+    gpool.ring_dt[0].copy_(torch.rand(gpool.ring_dt[0].shape, device="cuda", generator=g) * 0.2 + 1e-3)
+    rb = (torch.randn(gpool.ring_b[0].shape, device="cuda", generator=g) / math.sqrt(N)).to(torch.bfloat16)
+    gpool.ring_b[0].copy_(rb.float())
+    rows = torch.arange(b)
+    tstart = (c - 1 - rows % 3) + c * (rows % 2)              # 1-3 tokens before a boundary
+    gpool.t[0][slot_of_row.cuda()] = tstart.to(torch.int32).cuda()[:, None]
+    orc = SampledOracle(slot_of_row, c=c)
+    prm = O.make_params(H, G, N, seed=c)[0]
+    xs, dts, Bs, Cs = O.make_inputs(b, H, P, G, N, 3, seed=c)
+    A, D, dtb = prm["A"].cuda(), prm["D"].cuda(), prm["dt_bias"].cuda()
+    for s in range(3):
+        Br = O.rot_flat(Bs[s].reshape(b, G * N), prm["R"]).reshape(b, G, N)
+        Cr = O.rot_flat(Cs[s].reshape(b, G * N), prm["R"]).reshape(b, G, N)
+        orc.sync_from(gpool)
+        out = torch.zeros(b, H, P, device="cuda")
+        tiered_state_update(gpool, 0, xs[s].cuda(), dts[s].cuda(), A, Br.cuda(), Cr.cuda(), D, dtb, True,
+                            slot_of_row.to(torch.int32).cuda(), -1, out, None, 1e-3)
+        yo = O.tiered_step(orc.pool, torch.arange(b), xs[s], dts[s], Br, Cr, prm["A"], prm["D"], prm["dt_bias"], 1e-3)
+        torch.cuda.synchronize()
+        Hh.assert_y_close(out.cpu(), yo, f"c={c} step {s}")
+        assert int(((tstart + s + 1) % c == 0).sum()) == b // 3     # a third of the rows flushed
+        orc.compare(gpool)
+    assert int(gpool.status.item()) == 0

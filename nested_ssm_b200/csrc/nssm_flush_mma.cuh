@@ -33,15 +33,17 @@
 // (bounded) for its copies and MMAs in flight, frees its tensor memory and leaves.
 #pragma once
 
-#include "nssm_flush.cuh"
+#include "nssm_persistent.cuh"
 #include "nssm_tc.cuh"
 
 namespace nssm {
 
 constexpr int kFmThreads = 128;
+constexpr int kFmRowsPerThread = 8;   // batch rows one thread counts per pass (1024 per pass)
 constexpr uint32_t kFmTmemCols = 128;
 
-__host__ __device__ constexpr int fm_min_blocks(int c) { return c <= 8 ? 4 : c <= 16 ? 3 : 2; }
+// resident CTAs per SM the register budget is sized for (a row's NC values live in registers)
+__host__ __device__ constexpr int fm_min_blocks(int c, int nc) { return (c <= 8 && nc <= 96) ? 4 : c <= 16 ? 3 : 2; }
 // the three W pieces share one K range when 3c fits in two MMA K steps
 __host__ __device__ constexpr bool fm_packed(int c) { return 3 * c <= 32; }
 // K extent of the A tile(s): packed 3c rounded up to 16, else c per piece
@@ -83,6 +85,22 @@ __host__ inline FmLayout make_fm_layout(int maxb, int nst) {
   return L;
 }
 
+// e4m3 pairs of a 32-bit word -> four fp32 values (exact)
+__device__ __forceinline__ void fp8x4_to_f32(uint32_t w, float* v) {
+  const __half2_raw lo = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w & 0xffffu), __NV_E4M3);
+  const __half2_raw hi = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w >> 16), __NV_E4M3);
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&lo));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&hi));
+  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+}
+
+// four fp32 values (already divided by the row scale) -> four e4m3 codes, saturating
+__device__ __forceinline__ uint32_t f32x4_to_fp8x4(float a, float b, float c, float d) {
+  const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
+  const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(c, d), __NV_SATFINITE, __NV_E4M3);
+  return (lo & 0xffffu) | (hi << 16);
+}
+
 struct FmParams {
   StepParams sp;
   FmLayout L;
@@ -109,7 +127,7 @@ __device__ __forceinline__ void split3_bf16(float w, uint16_t& hi, uint16_t& mid
 }
 
 template <int PB, int NC, int CFIX, int P>
-__global__ void __launch_bounds__(kFmThreads, fm_min_blocks(CFIX)) flush_mma_kernel(const __grid_constant__ FmParams fp) {
+__global__ void __launch_bounds__(kFmThreads, fm_min_blocks(CFIX, NC)) flush_mma_kernel(const __grid_constant__ FmParams fp) {
   constexpr int NT = kFmThreads;
   constexpr int c = CFIX;
   constexpr int cp = (CFIX + 3) & ~3;
@@ -141,18 +159,62 @@ __global__ void __launch_bounds__(kFmThreads, fm_min_blocks(CFIX)) flush_mma_ker
   unsigned char* sA = sm + L.off_a;
   unsigned char* sB = sm + L.off_b;
 
-  // ---- the flushing rows, numbered in batch order; this CTA's share of their items
+  // ---- the flushing rows, numbered in batch order; this CTA's share of their items.  One
+  // pass: thread tid owns the contiguous rows [tid*R, tid*R + R) (R = ceil(batch / 128), at
+  // most kFmRowsPerThread; larger batches loop over blocks of 128 * R rows), loads all of their
+  // slots and then all of their token counts before using any (two memory round trips per
+  // block, not per 128 rows), and a block-wide exclusive scan of the per-thread counts numbers
+  // the flushing rows.  A launch where no row flushes leaves after that one pass.
   const int batch = fp.batch;
-  auto flush_row = [&](int b, int& slot) -> bool {
-    slot = p.idx ? p.idx[b] : b;
-    if (slot == p.pad || slot < 0 || slot >= p.S) return false;
-    const int tn = p.t[(int64_t)slot * H];
-    return tn > 0 && tn % c == 0;
+  const int R = min((batch + NT - 1) / NT, kFmRowsPerThread);
+  const int blk_rows = R * NT;
+  auto flags_of = [&](int r0, int* slots) -> uint32_t {   // bit k: row r0 + k flushes
+    int sl[kFmRowsPerThread];
+#pragma unroll
+    for (int k = 0; k < kFmRowsPerThread; ++k) {
+      const int b = r0 + k;
+      sl[k] = (k < R && b < batch) ? (p.idx ? p.idx[b] : b) : -1;
+    }
+    int tn[kFmRowsPerThread];
+#pragma unroll
+    for (int k = 0; k < kFmRowsPerThread; ++k) {
+      const bool v = sl[k] != p.pad && sl[k] >= 0 && sl[k] < p.S;
+      tn[k] = v ? p.t[(int64_t)sl[k] * H] : 0;
+      if (!v) sl[k] = -1;
+    }
+    uint32_t f = 0u;
+#pragma unroll
+    for (int k = 0; k < kFmRowsPerThread; ++k) {
+      if (sl[k] >= 0 && tn[k] > 0 && tn[k] % c == 0) f |= 1u << k;
+      if (slots) slots[k] = sl[k];
+    }
+    return f;
+  };
+  // exclusive prefix (over threads in order) of each thread's count, and the block total
+  auto block_scan = [&](int v, int& total) -> int {
+    int incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += n;
+    }
+    if (lane == 31) wcnt[warp] = incl;
+    __syncthreads();
+    int before = 0;
+    total = 0;
+    for (int w2 = 0; w2 < NT / 32; ++w2) {
+      const int n = wcnt[w2];
+      before += w2 < warp ? n : 0;
+      total += n;
+    }
+    __syncthreads();
+    return before + incl - v;
   };
   int nfl = 0;
-  for (int c0 = 0; c0 < batch; c0 += NT) {
-    int sl = -1;
-    nfl += __syncthreads_count(c0 + tid < batch && flush_row(c0 + tid, sl));
+  for (int bb = 0; bb < batch; bb += blk_rows) {
+    int tot = 0;
+    block_scan(__popc(flags_of(bb + tid * R, nullptr)), tot);
+    nfl += tot;
   }
   const int W = nfl * H;
   const int beg = (int)((long long)W * blockIdx.x / gridDim.x);
@@ -162,25 +224,19 @@ __global__ void __launch_bounds__(kFmThreads, fm_min_blocks(CFIX)) flush_mma_ker
   const int nb = (end - 1) / H - b0 + 1;
   {
     int base = 0;
-    for (int c0 = 0; c0 < batch && base < b0 + nb; c0 += NT) {   // uniform over the CTA
-      const int b = c0 + tid;
-      int slot = -1;
-      const bool f = b < batch && flush_row(b, slot);
-      const unsigned bal = __ballot_sync(0xffffffffu, f);
-      if (lane == 0) wcnt[warp] = __popc(bal);
-      __syncthreads();
-      int pre = 0, tot = 0;
-      for (int w = 0; w < NT / 32; ++w) {
-        const int n = wcnt[w];
-        pre += w < warp ? n : 0;
-        tot += n;
-      }
-      if (f) {
-        const int pos = base + pre + __popc(bal & ((1u << lane) - 1u));
-        if (pos >= b0 && pos < b0 + nb) bslot[pos - b0] = slot;
+    for (int bb = 0; bb < batch && base < b0 + nb; bb += blk_rows) {   // uniform over the CTA
+      int sl[kFmRowsPerThread];
+      const uint32_t f = flags_of(bb + tid * R, sl);
+      int tot = 0;
+      int pos = base + block_scan(__popc(f), tot);
+#pragma unroll
+      for (int k = 0; k < kFmRowsPerThread; ++k) {
+        if (f & (1u << k)) {
+          if (pos >= b0 && pos < b0 + nb) bslot[pos - b0] = sl[k];
+          ++pos;
+        }
       }
       base += tot;
-      __syncthreads();
     }
   }
   if (tid == 0) {
@@ -362,7 +418,7 @@ __global__ void __launch_bounds__(kFmThreads, fm_min_blocks(CFIX)) flush_mma_ker
 #pragma unroll
         for (int blk = 0; blk < NB; ++blk) tmem_ld16(taddr + (uint32_t)(blk * 16), v + 16 * blk);
       }
-      float m = 0.0f;
+      float mx[4] = {0.0f, 0.0f, 0.0f, 0.0f};   // independent partial maxima (no serial chain)
 #pragma unroll
       for (int blk = 0; blk < NB; ++blk) {
         const uint4 q4 = mine ? crow[blk] : make_uint4(0u, 0u, 0u, 0u);
@@ -376,12 +432,11 @@ __global__ void __launch_bounds__(kFmThreads, fm_min_blocks(CFIX)) flush_mma_ker
           const float2 d = __ffma2_rn(f2(qv[2], qv[3]), se2, f2(u[4 * wi + 2], u[4 * wi + 3]));
           u[4 * wi] = a.x; u[4 * wi + 1] = a.y;
           u[4 * wi + 2] = d.x; u[4 * wi + 3] = d.y;
+          mx[wi] = fmaxf(mx[wi], fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(d.x), fabsf(d.y))));
         }
-#pragma unroll
-        for (int e = 0; e < 16; e += 2)
-          m = fmaxf(m, fmaxf(fabsf(v[16 * blk + e]), fabsf(v[16 * blk + e + 1])));
       }
       if (mine) {
+        const float m = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
         const float sc = __fadd_rn(scale_div448(m), kScaleEps);
         const float rc = __frcp_rn(sc);
         reinterpret_cast<float*>(st + L.s_scale)[row] = sc;

@@ -12,7 +12,6 @@
 #include <string>
 
 #include "nssm_persistent.cuh"
-#include "nssm_flush.cuh"
 #include "nssm_flush_mma.cuh"
 #include "nssm_rot.cuh"
 #include "nssm_conv.cuh"
@@ -100,44 +99,6 @@ inline int launch_phase(const nssm::StepParams& sp, int batch, cudaStream_t st, 
   return NSSM_OK;
 }
 
-// The quad-row FLUSH kernel (fp8 cold, bf16 io, compile-time c and headdim); *done stays
-// false when its layout does not fit the device.
-template <int PB, int NC, int CFIX, int P>
-inline int launch_flush_quad(const nssm::StepParams& sp, int batch, cudaStream_t st, int sms, bool* done) {
-  *done = false;
-  const long long items = (long long)batch * sp.H;
-  auto fn = nssm::flush_quad_kernel<PB, NC, CFIX, P>;
-  constexpr int NT = nssm::fq_warps(P) * 32;
-  int optin = 0;
-  int rc = smem_optin(&optin);
-  if (rc) return rc;
-  for (int target = nssm::kFqMinBlocks; target >= 1; --target) {
-    long long grid = (long long)sms * target;
-    if (grid > items) grid = items;
-    const long long per_cta = (items + grid - 1) / grid;
-    const int maxb = (int)((per_cta + sp.H - 1) / sp.H) + 2;
-    nssm::FqParams fp{};
-    fp.sp = sp;
-    fp.batch = batch;
-    fp.polls = wait_polls();
-    int nst = 8;
-    for (; nst >= 2; --nst) {
-      fp.L = nssm::make_fq_layout<NC, CFIX, P>(maxb, (int)per_cta, nst);
-      if (fp.L.total <= optin && (long long)target * (fp.L.total + 1024) <= 228 * 1024) break;
-    }
-    if (nst < 2) continue;
-    int occ = 0;
-    rc = occupancy(reinterpret_cast<const void*>(fn), fp.L.total, NT, &occ);
-    if (rc) return rc;
-    if (occ >= target) {
-      fn<<<(unsigned)grid, NT, fp.L.total, st>>>(fp);
-      *done = true;
-      return cuda_check("flush_quad_kernel launch");
-    }
-  }
-  return NSSM_OK;
-}
-
 // The tensor-core FLUSH kernel (fp8 cold, bf16 io, c in {4, 8, 16, 64}, compile-time headdim);
 // *done stays false when its layout does not fit the device.
 template <int PB, int NC, int CFIX, int P>
@@ -148,7 +109,7 @@ inline int launch_flush_mma(const nssm::StepParams& sp, int batch, cudaStream_t 
   int optin = 0;
   int rc = smem_optin(&optin);
   if (rc) return rc;
-  for (int target = nssm::fm_min_blocks(CFIX); target >= 1; --target) {
+  for (int target = nssm::fm_min_blocks(CFIX, NC); target >= 1; --target) {
     long long grid = (long long)sms * target;
     if (grid > items) grid = items;
     const long long per_cta = (items + grid - 1) / grid;
@@ -167,7 +128,7 @@ inline int launch_flush_mma(const nssm::StepParams& sp, int batch, cudaStream_t 
     // fm_min_blocks CTAs), shared memory (checked above) and tensor memory (target x 128 of the
     // SM's 512 columns, so an allocation never waits).  The runtime's occupancy query reports
     // one CTA per SM for every kernel that allocates tensor memory, so it is not asked.
-    static_assert(nssm::fm_min_blocks(CFIX) * nssm::kFmTmemCols <= 512, "tensor memory per SM");
+    static_assert(nssm::fm_min_blocks(CFIX, NC) * nssm::kFmTmemCols <= 512, "tensor memory per SM");
     rc = ensure_smem_attr(reinterpret_cast<const void*>(fn));
     if (rc) return rc;
     fn<<<(unsigned)grid, nssm::kFmThreads, fp.L.total, st>>>(fp);
@@ -179,24 +140,14 @@ inline int launch_flush_mma(const nssm::StepParams& sp, int batch, cudaStream_t 
 
 // Both phases of one step.  The production configuration (fp8 cold, bf16 io) has
 // instances compiled for c in {4, 8, 16, 64} and headdim in {64, 80}; anything else
-// runs the instances that read c and headdim at run time.  Its FLUSH is the quad-row kernel
-// at c in {4, 8} (the ring in the stage) and the tensor-core kernel at c in {16, 64}
-// (NSSM_LEGACY_FLUSH builds keep the banded one for all).
+// runs the instances that read c and headdim at run time.  Its FLUSH is the tensor-core
+// kernel (NSSM_LEGACY_FLUSH builds keep the banded FLUSH phase of the persistent kernel).
 template <int PB, int NC, int COLD, bool IOBF, int CFIX, int RPWC>
 inline int launch_both(const nssm::StepParams& sp, int batch, cudaStream_t st, bool ring_ok, int sms) {
   bool done = false;
   int rc = launch_phase<PB, NC, COLD, IOBF, nssm::PH_STEP, CFIX, RPWC>(sp, batch, st, ring_ok, sms, &done);
   if (rc) return rc;
   if (!done) return launch_step<PB, NC, COLD, kTPR>(sp, batch, st);
-#ifdef NSSM_QUAD_FLUSH
-  if constexpr (COLD == nssm::COLD_FP8 && IOBF && (CFIX == 4 || CFIX == 8) && (RPWC == 8 || RPWC == 10) &&
-                NC % 16 == 0 && NC / 16 <= 8) {
-    if (ring_ok) {
-      rc = launch_flush_quad<PB, NC, CFIX, 8 * RPWC>(sp, batch, st, sms, &done);
-      if (rc || done) return rc;
-    }
-  }
-#endif
   if constexpr (COLD == nssm::COLD_FP8 && IOBF && (CFIX == 4 || CFIX == 8 || CFIX == 16 || CFIX == 64) &&
                 (RPWC == 8 || RPWC == 10) && NC % 16 == 0) {
 #ifndef NSSM_LEGACY_FLUSH

@@ -1,9 +1,11 @@
 """GPU parity at the benchmarked batch sizes (B = 256, 257, 448 rows; H=128, P=80, N=128, fp8
 cold, c=4) against the CPU oracle on a sample of rows.
 
-FLUSH counts and numbers the batch's flushing rows in passes of one CTA's threads (160 in the
-quad-row kernel at headdim 80, 256 in the banded one); past the first pass the running row
-number carried across passes decides which CTA replays which row.  Rows are independent, so the oracle only has to follow a sample of them (rows 0,
+FLUSH counts and numbers the batch's flushing rows before splitting their items over the grid
+(the tensor-core FLUSH: each of 128 threads takes a contiguous block of up to 8 rows and a
+block-wide scan numbers them; the banded FLUSH of other configurations: passes of 256 rows);
+a row past 256 is numbered from the rows before it, and that number decides which CTA
+replays it.  Rows are independent, so the oracle only has to follow a sample of them (rows 0,
 1, 255, 256, 257, 300, 447 where they exist and 32 random ones): before every step the
 oracle's copy of those rows is re-synced from the GPU pool, the whole batch steps on the GPU,
 the sampled rows step in the oracle, and y and the sampled pool rows are compared at the

@@ -58,7 +58,7 @@
 extern "C" {
 #endif
 
-#define NSSM_ABI_VERSION 1
+#define NSSM_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define NSSM_API __attribute__((visibility("default")))
@@ -140,6 +140,18 @@ typedef struct {
   void* workspace;        /* >= nssm_step_workspace_bytes() when R != NULL      */
   size_t workspace_bytes;
   int32_t* status;        /* optional device word, error bits OR-ed in          */
+  /* Optional gated RMS norm of y, fused into the step (the mixer's norm(y, gate) after the
+   * state op, scale/v4_native_decode.py:171): when norm_gate != NULL, out receives
+   * weight * round_io(h / sqrt(mean_group(h^2) + eps)) with h = round_out(y) * silu(gate)
+   * instead of y, exactly as nssm_gated_rmsnorm applied to the step's y.  A norm group must be
+   * one SSM group of one row: norm_group_size == (nheads / ngroups) * headdim. */
+  const void* norm_gate;  /* [batch][nheads*headdim] in out_dtype, or NULL         */
+  int64_t norm_gate_stride_b;
+  const void* norm_weight; /* [nheads*headdim]                                     */
+  int32_t norm_weight_dtype; /* F32 or BF16                                        */
+  int32_t norm_group_size;
+  float norm_eps;
+  int32_t _pad1;
 } nssm_step_args;
 
 /* Decode-token conv ahead of the state update, for one layer: the causal conv1d update of

@@ -15,7 +15,7 @@ from . import build as _build
 NSSM_OK, NSSM_ERR_INVALID, NSSM_ERR_UNSUPPORTED, NSSM_ERR_CUDA = 0, 1, 2, 3
 NSSM_F32, NSSM_BF16, NSSM_F8E4M3 = 0, 1, 2
 NSSM_MODE_STALE, NSSM_MODE_CORR, NSSM_MODE_COLDOFF = 0, 1, 2
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 EXPORTED = (
     "nssm_step_workspace_bytes", "nssm_tiered_step", "nssm_fresh_step", "nssm_prefill_split",
@@ -55,6 +55,9 @@ class NssmStepArgs(C.Structure):
         ("out", C.c_void_p), ("out_stride_b", C.c_int64), ("out_stride_h", C.c_int64),
         ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t),
         ("status", C.c_void_p),
+        ("norm_gate", C.c_void_p), ("norm_gate_stride_b", C.c_int64),
+        ("norm_weight", C.c_void_p), ("norm_weight_dtype", C.c_int32), ("norm_group_size", C.c_int32),
+        ("norm_eps", C.c_float), ("_pad1", C.c_int32),
     ]
 
 

@@ -13,6 +13,7 @@
 namespace nssm_host {
 
 thread_local std::string g_last_error;
+thread_local bool g_norm_fused = false;
 
 int fail(int code, const char* fmt, ...) {
   char buf[512];
@@ -243,6 +244,39 @@ void fill_inputs(const nssm_step_args* a, nssm::StepParams& sp) {
   sp.status = a->status;
 }
 
+// The gated norm requested with a step: validated here; fused into STEP when its gate rows
+// can be bulk-copied (16-byte aligned), else applied by the norm kernel after the step.
+int check_norm(const nssm_step_args* a, int H, int P, int G) {
+  if (!a->norm_gate) return NSSM_OK;
+  if (!a->norm_weight) return fail(NSSM_ERR_INVALID, "norm_gate given without norm_weight");
+  if (a->out_dtype != a->io_dtype)
+    return fail(NSSM_ERR_INVALID, "the fused norm needs out_dtype == io_dtype (gate and y share it)");
+  if (a->norm_weight_dtype != NSSM_F32 && a->norm_weight_dtype != NSSM_BF16)
+    return fail(NSSM_ERR_INVALID, "norm_weight_dtype must be F32 or BF16");
+  if (a->norm_group_size != (H / G) * P)
+    return fail(NSSM_ERR_INVALID, "norm_group_size %d must be one SSM group of a row, (nheads/ngroups)*headdim = %d",
+                a->norm_group_size, (H / G) * P);
+  if (a->out_stride_h != P) return fail(NSSM_ERR_INVALID, "the fused norm needs out rows [nheads*headdim] contiguous");
+  if (!(a->norm_eps >= 0.0f)) return fail(NSSM_ERR_INVALID, "norm_eps must be >= 0");
+  return NSSM_OK;
+}
+
+bool norm_fusable(const nssm_step_args* a) {
+  const int iob = io_bytes(a->io_dtype);
+  return aligned16(a->norm_gate) && (a->norm_gate_stride_b * iob) % 16 == 0;
+}
+
+int run_norm_after_step(const nssm_step_args* a, int H, int P, cudaStream_t st) {
+  nssm::NormParams np{};
+  np.y = a->out; np.y_sb = a->out_stride_b; np.gate = a->norm_gate; np.g_sb = a->norm_gate_stride_b;
+  np.weight = a->norm_weight; np.w_dtype = a->norm_weight_dtype; np.eps = a->norm_eps;
+  np.dim = H * P; np.gs = a->norm_group_size; np.dtype = a->out_dtype; np.out = a->out; np.o_sb = a->out_stride_b;
+  if (np.gs > nssm::kNormThreads * nssm::kNormMaxPer) return fail(NSSM_ERR_UNSUPPORTED, "norm group size %d too large", np.gs);
+  dim3 grid((unsigned)(np.dim / np.gs), (unsigned)a->batch);
+  nssm::gated_rmsnorm_kernel<<<grid, nssm::kNormThreads, 0, st>>>(np);   // in place: reads a group, then writes it
+  return cuda_check("gated_rmsnorm_kernel launch (after the step)");
+}
+
 }  // namespace
 
 extern "C" {
@@ -270,9 +304,18 @@ int nssm_tiered_step(const nssm_pool* pool, const nssm_step_args* args, void* st
   sp.ring_x = pool->ring_x; sp.ring_dt = pool->ring_dt; sp.ring_b = pool->ring_b;
   sp.S = pool->num_slots; sp.H = pool->nheads; sp.P = pool->headdim; sp.G = pool->ngroups; sp.c = pool->chunk;
   fill_inputs(args, sp);
+  rc = check_norm(args, pool->nheads, pool->headdim, pool->ngroups);
+  if (rc) return rc;
+  if (args->norm_gate && norm_fusable(args)) {
+    sp.ngate = args->norm_gate; sp.ngate_sb = args->norm_gate_stride_b;
+    sp.nweight = args->norm_weight; sp.nweight_dtype = args->norm_weight_dtype; sp.neps = args->norm_eps;
+  }
   rc = maybe_rotate(args, pool->ngroups, pool->dstate, sp, st);
   if (rc) return rc;
-  return dispatch(OP_STEP, pool->dstate, pool->hot_dim, pool->cold_dtype, &sp, args->batch, st);
+  g_norm_fused = false;
+  rc = dispatch(OP_STEP, pool->dstate, pool->hot_dim, pool->cold_dtype, &sp, args->batch, st);
+  if (rc || !args->norm_gate || g_norm_fused) return rc;
+  return run_norm_after_step(args, pool->nheads, pool->headdim, st);
 }
 
 int nssm_fresh_step(float* state, int32_t num_slots, int32_t nheads, int32_t headdim, int32_t dstate,
@@ -285,6 +328,7 @@ int nssm_fresh_step(float* state, int32_t num_slots, int32_t nheads, int32_t hea
   if (headdim > 128) return fail(NSSM_ERR_UNSUPPORTED, "headdim %d > 128", headdim);
   int rc = check_args(args, nheads);
   if (rc) return rc;
+  if (args->norm_gate) return fail(NSSM_ERR_INVALID, "the fused norm is a tiered-step option (nssm_fresh_step has none)");
   if (args->batch == 0) return NSSM_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   nssm::StepParams sp{};

@@ -83,6 +83,12 @@ struct StepParams {
   int64_t out_sb, out_sh;
   int out_dtype;
   int32_t* status;
+  // fused gated RMS norm of y (ngate != nullptr): out = weight * round(h * rstd_group)
+  const void* ngate;
+  int64_t ngate_sb;
+  const void* nweight;
+  int nweight_dtype;
+  float neps;
 };
 
 __device__ __forceinline__ float ld_io(const void* p, int64_t i, int dtype) {

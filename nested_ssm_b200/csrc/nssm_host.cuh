@@ -26,6 +26,8 @@ int sm_count(int* out);
 int smem_optin(int* out);
 uint32_t wait_polls();   // polls of a bounded pipeline wait (nssm_set_wait_polls)
 int inject_stuck();      // failure injection for tests (nssm_test_inject_stuck_copy)
+// set by the step dispatch when the gated norm ran fused into STEP (this thread's last call)
+extern thread_local bool g_norm_fused;
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
@@ -58,11 +60,12 @@ int launch_step(const nssm::StepParams& sp, int batch, cudaStream_t st) {
 // The persistent TMA-pipelined kernels move every per-item operand with 1-D bulk
 // copies, so they need 16-byte aligned rows: headdim % 4 == 0 and <= 80, x / B / C
 // bases and strides 16-byte aligned.  Anything else runs the simple kernel.
-template <int PB, int NC, int COLD, bool IOBF, int PHASE, int CFIX, int RPWC>
+template <int PB, int NC, int COLD, bool IOBF, int PHASE, int CFIX, int RPWC, bool NORM = false>
 inline int launch_phase(const nssm::StepParams& sp, int batch, cudaStream_t st, bool ring_ok, int sms, bool* done) {
   *done = false;
   const long long items = (long long)batch * sp.H;
-  auto fn = nssm::tiered_persistent_kernel<PB, NC, COLD, IOBF, PHASE, CFIX, RPWC>;
+  auto fn = nssm::tiered_persistent_kernel<PB, NC, COLD, IOBF, PHASE, CFIX, RPWC, NORM>;
+  const int hg = sp.H / sp.G;
   const int iob = IOBF ? 2 : 4;
   const int minb = PHASE == nssm::PH_STEP ? NSSM_STEP_P_MINB : NSSM_FLUSH_P_MINB;
   int optin = 0;
@@ -71,7 +74,8 @@ inline int launch_phase(const nssm::StepParams& sp, int batch, cudaStream_t st, 
   for (int target = minb; target >= 1; --target) {
     long long grid = (long long)sms * target;
     if (grid > items) grid = items;
-    const long long per_cta = (items + grid - 1) / grid;
+    // with the fused norm a CTA takes whole (row, group) units of hg items
+    const long long per_cta = NORM ? (items / hg + grid - 1) / grid * hg : (items + grid - 1) / grid;
     const int maxb = (int)((per_cta + sp.H - 1) / sp.H) + 2;
     nssm::PParams pp{};
     pp.sp = sp;
@@ -83,7 +87,7 @@ inline int launch_phase(const nssm::StepParams& sp, int batch, cudaStream_t st, 
     int nst = nssm::stages_for(PHASE);
     for (; nst >= 2; --nst) {
       pp.L = nssm::make_playout<PB, NC, COLD>(PHASE, sp.mode == NSSM_MODE_CORR, sp.P, sp.H, sp.c, iob, maxb,
-                                              (int)per_cta, ring_ok, nst);
+                                              (int)per_cta, ring_ok, nst, NORM ? hg : 0);
       if (pp.L.total <= optin && (long long)target * (pp.L.total + 1024) <= 228 * 1024) break;
     }
     if (nst < 2) continue;
@@ -145,7 +149,18 @@ inline int launch_flush_mma(const nssm::StepParams& sp, int batch, cudaStream_t 
 template <int PB, int NC, int COLD, bool IOBF, int CFIX, int RPWC>
 inline int launch_both(const nssm::StepParams& sp, int batch, cudaStream_t st, bool ring_ok, int sms) {
   bool done = false;
-  int rc = launch_phase<PB, NC, COLD, IOBF, nssm::PH_STEP, CFIX, RPWC>(sp, batch, st, ring_ok, sms, &done);
+  int rc = NSSM_OK;
+  // the fused norm runs in the production instances' STEP; elsewhere the step writes y and
+  // the caller of the dispatch applies the norm kernel (g_norm_fused stays false)
+  constexpr bool kNormable = COLD == nssm::COLD_FP8 && IOBF && RPWC > 0;
+  if constexpr (kNormable) {
+    if (sp.ngate) {
+      rc = launch_phase<PB, NC, COLD, IOBF, nssm::PH_STEP, CFIX, RPWC, true>(sp, batch, st, ring_ok, sms, &done);
+      if (rc) return rc;
+      g_norm_fused = done;
+    }
+  }
+  if (!done) rc = launch_phase<PB, NC, COLD, IOBF, nssm::PH_STEP, CFIX, RPWC>(sp, batch, st, ring_ok, sms, &done);
   if (rc) return rc;
   if (!done) return launch_step<PB, NC, COLD, kTPR>(sp, batch, st);
   if constexpr (COLD == nssm::COLD_FP8 && IOBF && (CFIX == 4 || CFIX == 8 || CFIX == 16 || CFIX == 64) &&

@@ -133,9 +133,9 @@ __device__ __forceinline__ float scale_div448(float m) {
 // Byte layout of the dynamic shared memory (computed on the host, passed in).
 struct PLayout {
   int stage_bytes;
-  int s_hot, s_cold, s_scale, s_x, s_b, s_c, s_rx, s_rb, s_rdt;   // inside a stage (0 size if unused)
+  int s_hot, s_cold, s_scale, s_x, s_b, s_c, s_rx, s_rb, s_rdt, s_gate;   // inside a stage (0 size if unused)
   int off_scal, off_head, off_yh, off_pc, off_sc, off_rcp, off_wsc, off_sw, off_rbw, off_fsc, off_bslot, off_bmeta,
-      off_bpos, off_bar;
+      off_bpos, off_gbuf, off_nslot, off_bar;
   int total;
   int nst;          // pipeline stages
   int rpw;          // headdim rows per warp band
@@ -150,7 +150,7 @@ constexpr int kScal = 8;   // per-item scalars (STEP): dt, dA, exp(dA), exp(glog
 
 template <int PB, int NC, int COLD>
 __host__ inline PLayout make_playout(int phase, bool corr, int P, int H, int c, int io_bytes, int maxb,
-                                     int maxitems, bool ring_in_stage, int nst) {
+                                     int maxitems, bool ring_in_stage, int nst, int norm_hg = 0) {
   constexpr int N = PB + NC;
   constexpr int ESZ = ColdTraits<COLD>::kBytes;
   constexpr int CPR = (NC * ESZ) / 16;
@@ -167,6 +167,7 @@ __host__ inline PLayout make_playout(int phase, bool corr, int P, int H, int c, 
   L.s_rx = o; o = al(o + (ring ? c * P * io_bytes : 0), 16);
   L.s_rb = o; o = al(o + (ring ? c * NC * 4 : 0), 16);      // ring B is fp32
   L.s_rdt = o; o = al(o + (ring ? ring_dt_stride(c) * 4 : 0), 16);
+  L.s_gate = o; o = al(o + (step && norm_hg ? P * io_bytes : 0), 16);   // fused norm: the item's gate
   L.stage_bytes = al(o, 128);
   L.rpw = (P + kPW - 1) / kPW;
   L.wsc_stride = al(2 * c + 2, 4);
@@ -186,8 +187,10 @@ __host__ inline PLayout make_playout(int phase, bool corr, int P, int H, int c, 
   L.off_bslot = t; t += maxb * 4;
   L.off_bmeta = t; t += maxb * 4;
   L.off_bpos = t; t += maxb * 4;
+  L.off_gbuf = t; t += norm_hg * P * 4;          // fused norm: h of a (row, group) [heads][P]
+  L.off_nslot = t; t += norm_hg ? 2 * kPW * 4 : 0;   // fused norm: per-warp sums of squares, 2 buffers
   t = al(t, 8);
-  L.off_bar = t; t += 2 * nst * 8;               // full[stages], empty[stages]
+  L.off_bar = t; t += 2 * nst * 8 + 8;           // full[stages], empty[stages], fused norm
   L.total = al(t, 128);
   L.maxb = maxb;
   L.maxitems = maxitems;
@@ -253,7 +256,11 @@ __device__ __forceinline__ void ld_row(const unsigned char* row, int n0, float* 
 // CFIX > 0 compiles the kernel for that flush period (unrolled replay loops) and
 // RPWC > 0 for headdim == 8 * RPWC (every warp band RPWC rows); 0 takes them from
 // the parameters.
-template <int PB, int NC, int COLD, bool IOBF, int PHASE, int CFIX, int RPWC>
+// NORM (STEP only) fuses the mixer's gated RMS norm into the y epilogue: CTAs take whole
+// (row, SSM group) units, every warp keeps h = round(y) * silu(gate) of its rows for the
+// group's heads in shared memory, and at the group's last head the warps' sums of squares meet
+// through an mbarrier (a bounded wait) and each warp writes its rows of weight * round(h * rstd).
+template <int PB, int NC, int COLD, bool IOBF, int PHASE, int CFIX, int RPWC, bool NORM = false>
 __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSSM_FLUSH_P_MINB)
     tiered_persistent_kernel(const __grid_constant__ PParams pp) {
   using Sh = StepShape<PB, NC, COLD>;
@@ -277,6 +284,7 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
   constexpr int kHR = kPair ? RPWC / 2 : 1;
   static_assert(32 % LPR == 0, "hot row chunks must tile a warp");
   static_assert(COLD != COLD_NONE && NC > 0, "tiered instances only");
+  static_assert(!NORM || PHASE == PH_STEP, "the norm is fused into STEP");
   static_assert(CE % 4 == 0 && PB % 4 == 0, "chunk shapes");
 
   const StepParams& p = pp.sp;
@@ -295,6 +303,7 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
   extern __shared__ __align__(128) unsigned char sm[];
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + L.off_bar);
   uint64_t* empty = full + L.nst;
+  uint64_t* nbar = empty + L.nst;   // fused norm: the warps' sums of squares of a group
   const float* scal = reinterpret_cast<const float*>(sm + L.off_scal);
   float* sA = reinterpret_cast<float*>(sm + L.off_head);
   float* yh = reinterpret_cast<float*>(sm + L.off_yh);
@@ -329,8 +338,13 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
     }
     W = nfl * H;
   }
-  const int beg = (int)((long long)W * blockIdx.x / gridDim.x);
-  const int end = (int)((long long)W * (blockIdx.x + 1) / gridDim.x);
+  int beg = (int)((long long)W * blockIdx.x / gridDim.x);
+  int end = (int)((long long)W * (blockIdx.x + 1) / gridDim.x);
+  if constexpr (NORM) {   // whole (row, group) units: a group's heads stay in one CTA
+    const int U = W / HG;
+    beg = (int)((long long)U * blockIdx.x / gridDim.x) * HG;
+    end = (int)((long long)U * (blockIdx.x + 1) / gridDim.x) * HG;
+  }
   if (beg >= end) return;
   const int b0 = beg / H;
   const int nb = (end - 1) / H - b0 + 1;
@@ -400,6 +414,7 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kPW);
     }
+    if (NORM) mbar_init(nbar, kPW);
     fence_mbar_init();
   }
   __syncthreads();
@@ -489,7 +504,11 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
     if (COLD == COLD_FP8) bytes += Pn * 4;
     if (STEP) bytes += (uint32_t)(Pn * PB * 4 + Pn * IOB + 2 * N * IOB);
     if (ring_st) bytes += (uint32_t)(c * Pn * IOB + c * NC * 4 + cp * 4);
+    if (NORM) bytes += (uint32_t)(Pn * IOB);
     mbar_expect_tx(&full[s], bytes + (stuck ? 16u : 0u));
+    if (NORM)
+      bulk_g2s(st + L.s_gate, static_cast<const char*>(p.ngate) + ((int64_t)b * p.ngate_sb + (int64_t)h * Pn) * IOB,
+               Pn * IOB, &full[s]);
     bulk_g2s(st + L.s_cold, static_cast<const char*>(p.cold) + sh * Pn * NC * ESZ, Pn * NC * ESZ, &full[s]);
     if (COLD == COLD_FP8) bulk_g2s(st + L.s_scale, p.scale + sh * Pn, Pn * 4, &full[s]);
     if (STEP) {
@@ -535,6 +554,8 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
   const int fcq = nrow > 0 ? lane / nrow : 0;
   const bool fok = nrow > 0 && fcq < fcw;
   bool ok = true;
+  float nss = 0.0f;     // fused norm: this lane's row's sum of h^2 over the group's heads so far
+  uint32_t npar = 0;    // fused norm: phase of nbar
 
   Cur q = start;
   first_valid(q);
@@ -705,8 +726,47 @@ __global__ void __launch_bounds__(kPT, PHASE == PH_STEP ? NSSM_STEP_P_MINB : NSS
           y += ycorr;
         }
         if (p.D) y = fmaf(xp, Dh, y);
-        st_io(p.out, (int64_t)b * p.out_sb + (int64_t)h * p.out_sh + row, p.out_dtype, y);
+        if constexpr (NORM) {
+          // h = round_out(y) * silu(gate), as the norm kernel computes it from the stored y
+          const float yq = p.out_dtype == NSSM_BF16 ? __bfloat162float(__float2bfloat16_rn(y)) : y;
+          const float z = ldv<IOBF>(st + L.s_gate, row);
+          const float hv = yq * (z / (1.0f + expf(-z)));
+          reinterpret_cast<float*>(sm + L.off_gbuf)[q.hr * Pn + row] = hv;
+          nss = fmaf(hv, hv, nss);
+        } else {
+          st_io(p.out, (int64_t)b * p.out_sb + (int64_t)h * p.out_sh + row, p.out_dtype, y);
+        }
         stv<IOBF>(p.ring_x, (sh * c + pos) * Pn + row, xp);
+      }
+      if constexpr (NORM) {
+        if (q.hr == HG - 1) {   // the group's last head: rstd over its HG * P channels
+          float ssw = nss;
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) ssw += __shfl_xor_sync(0xffffffffu, ssw, o);
+          float* nslot = reinterpret_cast<float*>(sm + L.off_nslot) + (npar ? kPW : 0);
+          if (lane == 0) {
+            nslot[warp] = ssw;
+            mbar_arrive(nbar);
+          }
+          if (!__all_sync(0xffffffffu, mbar_wait_bounded(nbar, npar, pp.polls))) { ok = false; break; }
+          float tot = 0.0f;
+#pragma unroll
+          for (int w2 = 0; w2 < kPW; ++w2) tot += nslot[w2];
+          const float r = 1.0f / sqrtf(tot / (float)(HG * Pn) + p.neps);
+          if (lane < nrow) {
+            const int row = r0 + lane;
+            const float* gb = reinterpret_cast<const float*>(sm + L.off_gbuf);
+            for (int hr = 0; hr < HG; ++hr) {
+              const int hh = g * HG + hr;
+              const float hv = gb[hr * Pn + row] * r;
+              const float hn = p.out_dtype == NSSM_BF16 ? __bfloat162float(__float2bfloat16_rn(hv)) : hv;
+              const float wv = ld_io(p.nweight, (int64_t)hh * Pn + row, p.nweight_dtype);
+              st_io(p.out, (int64_t)b * p.out_sb + (int64_t)hh * p.out_sh + row, p.out_dtype, wv * hn);
+            }
+          }
+          nss = 0.0f;
+          npar ^= 1u;
+        }
       }
       if (q.hr == 0) {   // the group's B_cold, once per group, spread over the warps
         for (int n = tid; n < NC; n += kPT)

@@ -94,9 +94,18 @@ def _decode(self, input_states, cache_params):
         Cv = Cv * mask.to(Cv.dtype)
     A = -torch.exp(self.A_log.float())
     y = torch.empty(b, H, P, dtype=dtype, device=input_states.device)
-    tiered_state_update(st["pool"], 0, x, dt[:, 0], A, Bv, Cv, self.D, self.dt_bias, True, st["slots"], -1, y,
-                        None, self.time_step_min, st["mode"])
-    scan_output = _norm(self, y.reshape(b, 1, I), gate)
+    norm = self.norm
+    if (all(hasattr(norm, a) for a in ("weight", "variance_epsilon", "group_size"))
+            and norm.group_size == (H // G) * P):
+        # the gated norm fused into the step (its group is one SSM group of a row)
+        tiered_state_update(st["pool"], 0, x, dt[:, 0], A, Bv, Cv, self.D, self.dt_bias, True, st["slots"], -1,
+                            y, None, self.time_step_min, st["mode"],
+                            norm=(gate[:, 0], norm.weight, norm.variance_epsilon))
+        scan_output = y.reshape(b, 1, I)
+    else:
+        tiered_state_update(st["pool"], 0, x, dt[:, 0], A, Bv, Cv, self.D, self.dt_bias, True, st["slots"], -1, y,
+                            None, self.time_step_min, st["mode"])
+        scan_output = _norm(self, y.reshape(b, 1, I), gate)
     return self.out_proj(scan_output.to(dtype))
 
 

@@ -154,11 +154,15 @@ def build_step_args(x, dt, A, B, C_, D=None, dt_bias=None, dt_softplus=True,
 
 def tiered_state_update(pool: TieredSlotPool, layer: int, x, dt, A, B, C_, D=None, dt_bias=None,
                         dt_softplus=True, state_batch_indices=None, pad_slot_id=-1, out=None,
-                        R=None, dt_min=DEFAULT_DT_MIN, mode="stale"):
+                        R=None, dt_min=DEFAULT_DT_MIN, mode="stale", norm=None):
     """One decode token of one layer on the tiered pool; returns ``out`` [b, H, P].
 
     Rows whose slot is ``pad_slot_id`` are skipped (their ``out`` rows untouched).
     ``R`` ([G, N, N]) rotates B and C first (fp32 accumulation, cast back to x's dtype).
+    ``norm = (gate [b, H*P], weight [H*P], eps)``: ``out`` receives the mixer's gated RMS norm
+    of y instead of y (scale/v4_native_decode.py:171; the same result as ``gated_rmsnorm`` on
+    the step's y), fused into the step; the norm group is one SSM group of a row, H/G*P
+    channels, and ``out`` must have x's dtype.
     """
     if x.dtype != pool.io_dtype:
         raise ValueError(f"x dtype {x.dtype} differs from the pool's io dtype {pool.io_dtype}")
@@ -167,6 +171,21 @@ def tiered_state_update(pool: TieredSlotPool, layer: int, x, dt, A, B, C_, D=Non
     a, out, keep = build_step_args(x, dt, A, B, C_, D, dt_bias, dt_softplus, state_batch_indices,
                                    pad_slot_id, out, R, dt_min, mode, pool.workspace, pool.status,
                                    nheads=pool.H)
+    if norm is not None:
+        gate, weight, eps = norm
+        b = x.shape[0]
+        g2 = gate.reshape(b, -1)
+        if g2.shape[1] != pool.H * pool.P or g2.stride(-1) != 1 or g2.dtype != out.dtype:
+            raise ValueError(f"norm gate must be [b, {pool.H * pool.P}] in out's dtype with a unit inner stride")
+        w = weight if weight.is_contiguous() else weight.contiguous()
+        if w.numel() != pool.H * pool.P or w.dtype not in (torch.bfloat16, torch.float32):
+            raise ValueError("norm weight must have H*P bf16 / fp32 entries")
+        _require_cuda(g2, w)
+        a.norm_gate, a.norm_gate_stride_b = g2.data_ptr(), g2.stride(0)
+        a.norm_weight, a.norm_weight_dtype = w.data_ptr(), nssm_dtype(w.dtype)
+        a.norm_group_size = (pool.H // pool.G) * pool.P
+        a.norm_eps = float(eps)
+        keep = keep + (g2, w)
     lib = _lib.load()
     _lib.check(lib.nssm_tiered_step(C.byref(pool.struct(layer)), C.byref(a), _stream(x.device)))
     return out

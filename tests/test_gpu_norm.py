@@ -31,8 +31,8 @@ def test_gated_rmsnorm_matches_oracle(dtype, wdt):
 def _fused_vs_separate(b, S, gate_offset, seed):
     """Two pools from the same state take the same token: one through the step with the fused
     norm, one through the plain step and then gated_rmsnorm.  The pools must end bit-identical
-    (the norm changes only what goes to out) and the outputs agree within one bf16 ulp (the sum
-    of squares is accumulated in another order)."""
+    (the norm changes only what goes to out) and the outputs agree within two bf16 ulps, rarely
+    differing at all (the sum of squares is accumulated in another order)."""
     import math
     from nested_ssm_b200 import TieredSlotPool, gated_rmsnorm, prefill_split, tiered_state_update
     H, P, N, G = 128, 80, 128, 8
@@ -64,8 +64,10 @@ def _fused_vs_separate(b, S, gate_offset, seed):
         want = gated_rmsnorm(y.reshape(b, H * P), gate, w, 1e-5, (H // G) * P).reshape(b, H, P)
         torch.cuda.synchronize()
         got, want = y_f.float().cpu(), want.float().cpu()
+        # a one-ulp flip of round(h * rstd) (the sums of squares run in another order) is then
+        # multiplied by the weight and rounded again: at most two bf16 ulps of the output
         err = (got - want)[live].abs()
-        bound = want[live].abs() * 2.0 ** -7 + 1e-6
+        bound = want[live].abs() * 2.0 ** -6 + 1e-6
         assert bool((err <= bound).all()), f"step {s}: fused norm off by {float((err / bound).max()):.2f}x"
         assert float((err > 0).float().mean()) <= 2e-2
         assert bool((got[~live] == 0).all()), "padded rows must be left untouched"

@@ -76,6 +76,12 @@ def parse():
                     help="skip the same-box run of the reference's own GPU decode arms")
     ap.add_argument("--reference-gpu-leg-only", action="store_true", help=argparse.SUPPRESS)
     ap.add_argument("--no-multi-gpu-check", action="store_true")
+    ap.add_argument("--model-e2e", action="store_true",
+                    help="only the end-to-end model decode (reduced BASELINE config 4) and print its JSON")
+    ap.add_argument("--model-batch", type=int, default=448)
+    ap.add_argument("--model-prompt", type=int, default=8)
+    ap.add_argument("--model-gen", type=int, default=32)
+    ap.add_argument("--model-arms", default="ours,reference,hf")
     return ap.parse_args()
 
 
@@ -929,6 +935,108 @@ def multi_gpu_check(args, rank: int, ws: int):
                      "bit-identical to one GPU serving the whole global batch"}
 
 
+def nemotron_h_9b(device="cuda", chunk_size=8):
+    """The BASELINE's end-to-end architecture (Nemotron-H 9B), random init, bf16: hidden 4480,
+    56 layers = 27 Mamba2 (128 heads x 80, d_state 128, 8 groups, conv 4) + 4 GQA attention
+    (40 q / 8 kv heads of 128) + 25 ReLU^2 MLP (intermediate 15680), vocab 131072, weights
+    ~N(0, 0.02).  transformers 5.5's NemotronH has no dense-MLP block type ("-" in the published
+    layout), so those blocks are built as NemotronHMLP under the "moe" type, whose block forward is
+    the same plain mixer(hidden) call and whose attention mask is None.  ``chunk_size`` is the
+    prefill scan's chunk, which the decode does not use: the model's own naive prefill pads the
+    prompt to whole chunks and holds fp32 products of (batch, chunks, chunk, chunk, heads, d_state)
+    and of (batch, padded prompt, heads, headdim, d_state) -- 1.9 GB and 19 GB at B = 448 with an
+    8-token prompt and chunk 8, but 481 GB for the first at the published chunk 128."""
+    from transformers import NemotronHConfig, NemotronHForCausalLM
+    from transformers.models.nemotron_h import modeling_nemotron_h as MH
+    layout = "M-M-M-MM-M-M-M*-M-M-M*-M-M-M-M*-M-M-M-M*-M-MM-M-M-M-M-M-"   # the published 9B-v2 layout
+    kinds = {"M": "mamba", "*": "attention", "-": "moe"}
+    cfg = NemotronHConfig(hidden_size=4480, layers_block_type=[kinds[ch] for ch in layout],
+                          num_hidden_layers=len(layout), mamba_num_heads=128, mamba_head_dim=80,
+                          ssm_state_size=128, n_groups=8, conv_kernel=4, expand=2, intermediate_size=15680,
+                          mlp_hidden_act="relu2", num_attention_heads=40, num_key_value_heads=8, head_dim=128,
+                          vocab_size=131072, chunk_size=chunk_size, initializer_range=0.02)
+    saved = MH.MIXER_TYPES["moe"]
+    MH.MIXER_TYPES["moe"] = lambda config, layer_idx=None: MH.NemotronHMLP(config)
+    try:
+        with torch.device(device):
+            model = NemotronHForCausalLM(cfg)
+    finally:
+        MH.MIXER_TYPES["moe"] = saved
+    return model.to(torch.bfloat16).eval()
+
+
+def model_e2e(args, device="cuda", build=None):
+    """Reduced BASELINE config 4 on one GPU: decode tokens/s of a random-init Nemotron-H 9B (bf16,
+    weights ~N(0, 0.02)) with seeded per-group rotations (the reference's ActRotMask around every
+    mixer's activation), B sequences of `--model-prompt` random tokens, `--model-gen` greedy
+    tokens through transformers' generate.  Decode time = generate(gen + 1) - generate(1), so the
+    prefill cancels; the prefill is the model's own in every arm (this image has no mamba_ssm, and
+    the lean chunk-scan prefill wants chunk 128).  Arms on the same model and box: `ours`
+    (nested_ssm_b200.hf.install: conv step, tiered step with the fused norm; fp8 cold, c = 4),
+    `reference` (the reference's own scale/v4_native_decode.install, unmodified from baseline/_ref;
+    bf16 cold, its default), `hf` (transformers' own decode over the fresh full state)."""
+    if not os.path.exists(os.path.join(REF_DIR, "nemotron_retrofit.py")):
+        return {"unavailable": "baseline/_ref is not installed (baseline/install.sh): the rotation wrapper is the "
+                               "reference's ActRotMask"}
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    import nemotron_retrofit as NR   # noqa: E402  (the reference's modules, unmodified)
+    import v4_native_decode as V4   # noqa: E402
+    build = build or nemotron_h_9b
+    Bm, T, K = args.model_batch, args.model_prompt, args.model_gen
+    out = {"config": {"workload": "reduced BASELINE config 4: random-init Nemotron-H 9B architecture, bf16, "
+                                  f"B={Bm}, prompt {T} random tokens, {K} greedy decode tokens "
+                                  "(the config's 4096 / 512 reduced), one GPU, decode = generate(K+1) - generate(1)",
+                      "batch": Bm, "prompt": T, "gen": K}, "arms": {}}
+    for arm in [a for a in args.model_arms.split(",") if a]:
+        torch.manual_seed(0)
+        model = build(device)
+        g = torch.Generator(device=device).manual_seed(1)
+        for m in model.modules():
+            if type(m).__name__ == "NemotronHMamba2Mixer":
+                act = NR.ActRotMask(m.act, m.intermediate_size, m.n_groups, m.ssm_state_size).to(device)
+                q = torch.linalg.qr(torch.randn(m.n_groups, m.ssm_state_size, m.ssm_state_size, device=device,
+                                                generator=g))[0]
+                act.R.data.copy_(q)
+                m.act = act
+        if arm == "ours":
+            from nested_ssm_b200 import hf as HF
+            HF.install(model, pb=32, c=4, cold="fp8")
+        elif arm == "reference":
+            V4.install(model, pb=32, c=4)
+            for m in model.modules():
+                if hasattr(m, "v4cfg"):
+                    m.v4cfg["lean_prefill"] = 0   # its lean prefill imports mamba_ssm, absent here
+        ids = torch.randint(1000, 30000, (Bm, T), device=device, generator=g)
+        gk = dict(do_sample=False, pad_token_id=0, eos_token_id=None)
+        sync = torch.cuda.synchronize if device == "cuda" else (lambda: None)
+
+        def gen(n):
+            sync()
+            t0 = time.perf_counter()
+            with torch.no_grad():
+                toks = model.generate(ids, max_new_tokens=n, **gk)
+            sync()
+            return time.perf_counter() - t0, toks
+
+        try:
+            gen(2)                                   # warm-up (kernels, allocator)
+            (t1, _), (tk, toks) = gen(1), gen(K + 1)
+            dec = (tk - t1) / K
+            res = {"decode_ms_per_token": round(dec * 1e3, 2), "decode_tokens_per_s": round(Bm / dec, 1),
+                   "prefill_s": round(t1, 3), "tokens_crc": int(toks[:, T:].to(torch.int64).sum())}
+            if device == "cuda":
+                res["peak_gb"] = round(torch.cuda.max_memory_allocated() / 1e9, 1)
+            out["arms"][arm] = res
+        except torch.cuda.OutOfMemoryError as e:
+            out["arms"][arm] = {"unavailable": f"out of memory: {str(e)[:160]}"}
+        del model
+        if device == "cuda":
+            torch.cuda.empty_cache()
+            torch.cuda.reset_peak_memory_stats()
+    return out
+
+
 # --------------------------------------------------------------------------
 # CPU legs (the oracle port -- the reference's own path is Python/torch)
 # --------------------------------------------------------------------------
@@ -1035,6 +1143,11 @@ def main():
         return 0
     if args.reference_gpu_leg_only:
         print(json.dumps(reference_gpu_leg()), flush=True)
+        return 0
+    if args.model_e2e:
+        if not torch.cuda.is_available():
+            raise SystemExit("bench.py --model-e2e needs a CUDA device")
+        print(json.dumps({"model_e2e": model_e2e(args)}), flush=True)
         return 0
     rank, ws, local = dist_init()
     if not torch.cuda.is_available():

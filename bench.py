@@ -76,6 +76,7 @@ def parse():
                     help="skip the same-box run of the reference's own GPU decode arms")
     ap.add_argument("--reference-gpu-leg-only", action="store_true", help=argparse.SUPPRESS)
     ap.add_argument("--no-multi-gpu-check", action="store_true")
+    ap.add_argument("--no-selfspec", action="store_true")
     ap.add_argument("--model-e2e", action="store_true",
                     help="only the end-to-end model decode (reduced BASELINE config 4) and print its JSON")
     ap.add_argument("--model-batch", type=int, default=448)
@@ -796,6 +797,75 @@ def graph_of_steps(wl: Workload, k0: int):
     return g
 
 
+def time_selfspec(args, rank: int, ws: int, step_ms: float):
+    """The self-speculative cycle at the state-op level (what scale/bench_selfspec_e2e.py times
+    for the whole model): c hot-only draft tokens (rotation + draft step per layer), one verify
+    of the c tokens and the commit of all of them (which flushes: the cycle starts at a chunk
+    boundary), over every layer, B sequences, against c ordinary decode steps.  All drafts
+    accepted, as the reference's mech(c); a fresh workload so the cycle starts at phase 0."""
+    from nested_ssm_b200 import commit_state_update, draft_state_update, verify_state_update
+    wl = Workload(args, rank)
+    L, B, c, NI = wl.L, wl.B, args.chunk, Workload.NI
+    draft = wl.pool.new_draft()
+    xs = [torch.stack([wl.x[j % NI, l] for j in range(c)], 1) for l in range(L)]
+    dts = [torch.stack([wl.dt[j % NI, l] for j in range(c)], 1) for l in range(L)]
+    Bs = [torch.stack([wl.BC[j % NI, l, :B] for j in range(c)], 1).view(B, c, G, N) for l in range(L)]
+    Cs = [torch.stack([wl.BC[j % NI, l, B:] for j in range(c)], 1).view(B, c, G, N) for l in range(L)]
+    yd = torch.empty(B, H, P, dtype=torch.bfloat16, device="cuda")
+    yv = torch.empty(B, c, H, P, dtype=torch.bfloat16, device="cuda")
+    accept = torch.full((B,), c, dtype=torch.int32, device="cuda")
+
+    def drafts():
+        for j in range(c):
+            i = j % NI
+            for l in range(L):
+                draft_state_update(wl.pool, l, draft[l], wl.x[i, l], wl.dt[i, l], wl.A[l],
+                                   wl.BC[i, l, :B].view(B, G, N), wl.BC[i, l, B:].view(B, G, N), wl.D[l], wl.dtb[l],
+                                   True, wl.slots, -1, yd, wl.R[l], 1e-3, from_pool=(j == 0))
+
+    def verify():
+        for l in range(L):
+            verify_state_update(wl.pool, l, xs[l], dts[l], wl.A[l], Bs[l], Cs[l], wl.D[l], wl.dtb[l], True, wl.slots,
+                                -1, yv, wl.R[l], 1e-3)
+
+    def commit():
+        for l in range(L):
+            commit_state_update(wl.pool, l, accept, xs[l], dts[l], wl.A[l], Bs[l], wl.dtb[l], True, wl.slots, -1,
+                                wl.R[l], 1e-3)
+
+    for _ in range(2):   # warm-up cycles
+        drafts()
+        verify()
+        commit()
+    reps = 4
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4 * reps)]
+    barrier(ws)
+    torch.cuda.synchronize()
+    for r in range(reps):
+        ev[4 * r].record()
+        drafts()
+        ev[4 * r + 1].record()
+        verify()
+        ev[4 * r + 2].record()
+        commit()
+        ev[4 * r + 3].record()
+    torch.cuda.synchronize()
+    d_ms = max_over_ranks(statistics.mean(ev[4 * r].elapsed_time(ev[4 * r + 1]) for r in range(reps)) / c, ws)
+    v_ms = max_over_ranks(statistics.mean(ev[4 * r + 1].elapsed_time(ev[4 * r + 2]) for r in range(reps)), ws)
+    c_ms = max_over_ranks(statistics.mean(ev[4 * r + 2].elapsed_time(ev[4 * r + 3]) for r in range(reps)), ws)
+    barrier(ws)
+    wl.pool.check_status()
+    del wl, draft, xs, dts, Bs, Cs
+    torch.cuda.empty_cache()
+    cycle = c * d_ms + v_ms + c_ms
+    return {"chunk": c, "draft_tokens": c, "batch_per_gpu": B, "layers": L,
+            "draft_ms_per_token": round(d_ms, 4), "verify_ms": round(v_ms, 4), "commit_ms_incl_flush": round(c_ms, 4),
+            "cycle_ms": round(cycle, 4), "decode_step_ms": round(step_ms, 4),
+            "mech_speedup_all_accepted": round(c * step_ms / cycle, 3),
+            "note": "state op only, every layer (rotation included); the model-level gain of self-speculation "
+                    "comes from the verify reading the weights once for c tokens, which this leg does not model"}
+
+
 # The reference's own measurement of this configuration (scale/bench_v4_decode.json: B=256,
 # pb=32, c=4, its fp8-cold arm), ms per 27-layer step.
 REF_CONFIG1_FP8_MS = 39.0069
@@ -1258,6 +1328,8 @@ def main():
     ragged = None if args.no_ragged else time_ragged(args, rank, ws)
     torch.cuda.empty_cache()
     config1 = None if args.no_config1 else time_config1(args, rank, ws)
+    torch.cuda.empty_cache()
+    selfspec = None if args.no_selfspec else time_selfspec(args, rank, ws, ms)
     mcheck = None if (ws == 1 or args.no_multi_gpu_check) else multi_gpu_check(args, rank, ws)
     ref_gpu = None
     if rank == 0 and ws == 1 and not args.no_reference_gpu:
@@ -1300,6 +1372,7 @@ def main():
             "prefill_scan": prefill,
             "ragged": ragged,
             "config1": config1,
+            "selfspec": selfspec,
             "reference_gpu": ref_gpu,
             "multi_gpu_check": mcheck,
             "clocks": clocks,

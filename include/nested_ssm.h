@@ -44,6 +44,10 @@
  *        mamba_chunk_scan_combined (called at scale/v4_native_decode.py:209-216)
  *        with z = NULL and the final states returned; its final state feeds
  *        nssm_prefill_split.
+ *  - nssm_draft_step / nssm_verify_step / nssm_commit_step: the hot-only self-speculative
+ *        draft (install(cold="off"), scale/v4_fused_decode.py:49-55 and :140-142) and the
+ *        draft -> verify -> accept cycle that scale/bench_selfspec_e2e.py:1-83 times, on the
+ *        tiered state (the reference verifies against a full fp32 state it keeps besides).
  *  - nssm_conv_step    : causal_conv1d_update + split + the post-conv R rotation of
  *        _v4_fused_decode (scale/v4_fused_decode.py:39-48); the HF decode branch's
  *        conv-state roll + weighted sum + act (scale/v4_native_decode.py:36-49).
@@ -58,7 +62,7 @@
 extern "C" {
 #endif
 
-#define NSSM_ABI_VERSION 2
+#define NSSM_ABI_VERSION 3
 
 #if defined(__GNUC__)
 #define NSSM_API __attribute__((visibility("default")))
@@ -327,9 +331,62 @@ NSSM_API uint32_t nssm_set_wait_polls(uint32_t polls);
  * the reference. */
 NSSM_API int32_t nssm_test_inject_stuck_copy(int32_t enable);
 
+/* ---- self-speculative decoding ----------------------------------------------------------
+ * A cycle per layer: nssm_draft_step for each draft token (the hot-only model), then one
+ * nssm_verify_step over the n drafted tokens (the y the tiered model gives each of them),
+ * then nssm_commit_step with the number of tokens each row accepted.  Verify is read-only on
+ * the pool; commit of k tokens leaves the pool exactly as k nssm_tiered_step calls with the
+ * same inputs would (the same kernels' arithmetic, FLUSH included when the k tokens complete a
+ * chunk).  A verify / commit window may end on a chunk boundary but not cross it:
+ * (t % chunk) + ntok <= chunk for every row, so a cycle drafts chunk - t % chunk tokens at most.
+ * Rows that break this, or whose accept count is outside [0, ntok], are skipped and set bit 2
+ * of *status. */
+
+/* Token strides of the multi-token inputs: with nssm_step_args describing token 0 of every
+ * row (x_stride_b etc. between rows), token j of row b is at + b*stride_b + j*stride_t. */
+typedef struct {
+  int32_t ntok;          /* tokens per row (>= 1)                                       */
+  int32_t _pad0;
+  int64_t x_stride_t;    /* x   [batch][ntok][nheads][headdim]                          */
+  int64_t dt_stride_t;   /* dt  [batch][ntok][nheads]                                   */
+  int64_t B_stride_t;    /* B   [batch][ntok][ngroups][dstate]                          */
+  int64_t C_stride_t;    /* C   [batch][ntok][ngroups][dstate] (verify)                 */
+  int64_t out_stride_t;  /* out [batch][ntok][nheads][headdim] (verify)                 */
+  const int32_t* accept; /* commit: [batch] tokens each row keeps, 0..ntok (device)     */
+} nssm_token_args;
+
+/* Workspace of nssm_verify_step / nssm_commit_step: the rotated B and C of batch*ntok rows
+ * when R != NULL, and (commit) one int32 per row. */
+NSSM_API size_t nssm_spec_workspace_bytes(int32_t batch, int32_t ntok, int32_t ngroups, int32_t dstate,
+                                          int32_t io_dtype, int32_t has_rotation);
+
+/* One draft token of the hot-only model: draft [num_slots][nheads][headdim][hot_dim] fp32
+ * (indexed by slot like the pool) <- h exp(dt A) + (dt B_hot) x, with h read from the pool's
+ * hot slice when from_pool != 0 (the cycle's first draft token) and from draft otherwise;
+ * out <- C_hot . h + D x.  The pool is not written.  args->mode and the norm are not used
+ * (norm_gate must be NULL); R, dt_softplus, dt_bias and dt_min as in nssm_tiered_step. */
+NSSM_API int nssm_draft_step(const nssm_pool* pool, float* draft, int32_t from_pool, const nssm_step_args* args,
+                             void* stream);
+
+/* y of tok->ntok tokens per row from the committed tiered state, exactly as that many
+ * successive nssm_tiered_step calls would read them (modes STALE and COLDOFF; CORR is not
+ * supported).  Read-only on the pool.  args->batch rows; args->workspace of
+ * nssm_spec_workspace_bytes() when R != NULL (B and C rows must then be token-contiguous:
+ * B_stride_b == ntok * B_stride_t, likewise C). */
+NSSM_API int nssm_verify_step(const nssm_pool* pool, const nssm_step_args* args, const nssm_token_args* tok,
+                              void* stream);
+
+/* Make the first tok->accept[b] of tok->ntok tokens of row b permanent (hot slice, ring, glog,
+ * t, and the FLUSH of rows whose chunk they complete).  Inputs x, dt, B (and R) as given to
+ * nssm_verify_step; C, D, out and mode are not used.  args->workspace of
+ * nssm_spec_workspace_bytes() bytes is always needed. */
+NSSM_API int nssm_commit_step(const nssm_pool* pool, const nssm_step_args* args, const nssm_token_args* tok,
+                              void* stream);
+
 /* sizeof of the argument structs, for binding checks. */
 NSSM_API size_t nssm_sizeof_pool(void);
 NSSM_API size_t nssm_sizeof_step_args(void);
+NSSM_API size_t nssm_sizeof_token_args(void);
 
 NSSM_API int32_t nssm_abi_version(void);
 NSSM_API const char* nssm_last_error(void);

@@ -9,7 +9,9 @@ the host; the work runs in hand-written CUDA behind the C ABI of
 """
 from ._lib import load as load_library, supported_hot_dims  # noqa: F401
 from .ops import (  # noqa: F401
+    commit_state_update,
     conv_step,
+    draft_state_update,
     gated_rmsnorm,
     mamba_chunk_scan_combined,
     materialize,
@@ -18,6 +20,7 @@ from .ops import (  # noqa: F401
     rot_flat,
     selective_state_update,
     tiered_state_update,
+    verify_state_update,
 )
 from .pool import TieredSlotPool  # noqa: F401
 

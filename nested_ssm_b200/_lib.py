@@ -15,7 +15,7 @@ from . import build as _build
 NSSM_OK, NSSM_ERR_INVALID, NSSM_ERR_UNSUPPORTED, NSSM_ERR_CUDA = 0, 1, 2, 3
 NSSM_F32, NSSM_BF16, NSSM_F8E4M3 = 0, 1, 2
 NSSM_MODE_STALE, NSSM_MODE_CORR, NSSM_MODE_COLDOFF = 0, 1, 2
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 EXPORTED = (
     "nssm_step_workspace_bytes", "nssm_tiered_step", "nssm_fresh_step", "nssm_prefill_split",
@@ -23,6 +23,8 @@ EXPORTED = (
     "nssm_sizeof_step_args", "nssm_abi_version", "nssm_last_error", "nssm_tiered_step_static",
     "nssm_conv_step", "nssm_sizeof_conv_args", "nssm_gated_rmsnorm", "nssm_chunk_scan",
     "nssm_sizeof_scan_args", "nssm_set_wait_polls", "nssm_test_inject_stuck_copy",
+    "nssm_spec_workspace_bytes", "nssm_draft_step", "nssm_verify_step", "nssm_commit_step",
+    "nssm_sizeof_token_args",
 )
 
 
@@ -58,6 +60,14 @@ class NssmStepArgs(C.Structure):
         ("norm_gate", C.c_void_p), ("norm_gate_stride_b", C.c_int64),
         ("norm_weight", C.c_void_p), ("norm_weight_dtype", C.c_int32), ("norm_group_size", C.c_int32),
         ("norm_eps", C.c_float), ("_pad1", C.c_int32),
+    ]
+
+
+class NssmTokenArgs(C.Structure):
+    _fields_ = [
+        ("ntok", C.c_int32), ("_pad0", C.c_int32),
+        ("x_stride_t", C.c_int64), ("dt_stride_t", C.c_int64), ("B_stride_t", C.c_int64),
+        ("C_stride_t", C.c_int64), ("out_stride_t", C.c_int64), ("accept", C.c_void_p),
     ]
 
 
@@ -144,6 +154,11 @@ def load(auto_build: bool = True) -> C.CDLL:
             "nssm_last_error": (C.c_char_p, []),
             "nssm_set_wait_polls": (C.c_uint32, [C.c_uint32]),
             "nssm_test_inject_stuck_copy": (i32, [i32]),
+            "nssm_spec_workspace_bytes": (sz, [i32, i32, i32, i32, i32, i32]),
+            "nssm_draft_step": (C.c_int, [P_pool, vp, i32, P_args, vp]),
+            "nssm_verify_step": (C.c_int, [P_pool, P_args, C.POINTER(NssmTokenArgs), vp]),
+            "nssm_commit_step": (C.c_int, [P_pool, P_args, C.POINTER(NssmTokenArgs), vp]),
+            "nssm_sizeof_token_args": (sz, []),
         }
         for name, (res, args) in sig.items():
             fn = getattr(lib, name)
@@ -152,7 +167,8 @@ def load(auto_build: bool = True) -> C.CDLL:
             raise RuntimeError(f"libnested_ssm ABI {lib.nssm_abi_version()} != binding {ABI_VERSION}")
         if (lib.nssm_sizeof_pool() != C.sizeof(NssmPool) or lib.nssm_sizeof_step_args() != C.sizeof(NssmStepArgs)
                 or lib.nssm_sizeof_conv_args() != C.sizeof(NssmConvArgs)
-                or lib.nssm_sizeof_scan_args() != C.sizeof(NssmScanArgs)):
+                or lib.nssm_sizeof_scan_args() != C.sizeof(NssmScanArgs)
+                or lib.nssm_sizeof_token_args() != C.sizeof(NssmTokenArgs)):
             raise RuntimeError("libnested_ssm struct layout differs from the ctypes binding")
         _lib = lib
         return lib

@@ -277,9 +277,140 @@ int run_norm_after_step(const nssm_step_args* a, int H, int P, cudaStream_t st) 
   return cuda_check("gated_rmsnorm_kernel launch (after the step)");
 }
 
+void fill_pool(const nssm_pool* pool, nssm::StepParams& sp) {
+  sp.hot = pool->hot; sp.cold = pool->cold; sp.scale = pool->cold_scale;
+  sp.glog = pool->glog; sp.t = pool->t;
+  sp.ring_x = pool->ring_x; sp.ring_dt = pool->ring_dt; sp.ring_b = pool->ring_b;
+  sp.S = pool->num_slots; sp.H = pool->nheads; sp.P = pool->headdim; sp.G = pool->ngroups; sp.c = pool->chunk;
+}
+
+// Checks shared by the self-speculative entry points; fills sp (pool + token-0 inputs) and the
+// token strides of q.
+int spec_prepare(const nssm_pool* pool, const nssm_step_args* a, const nssm_token_args* tok, nssm::StepParams& sp,
+                 nssm::SpecParams& q) {
+  int rc = check_pool(pool);
+  if (rc) return rc;
+  rc = check_args(a, pool->nheads);
+  if (rc) return rc;
+  if (a->io_dtype != pool->io_dtype)
+    return fail(NSSM_ERR_INVALID, "args io_dtype %d differs from the pool's ring dtype %d", a->io_dtype, pool->io_dtype);
+  if (a->norm_gate) return fail(NSSM_ERR_INVALID, "the fused norm is a nssm_tiered_step option");
+  if (tok) {
+    if (tok->ntok < 1) return fail(NSSM_ERR_INVALID, "ntok %d < 1", tok->ntok);
+    if (tok->ntok > pool->chunk)
+      return fail(NSSM_ERR_INVALID, "ntok %d > chunk %d: a window cannot cross a chunk boundary", tok->ntok, pool->chunk);
+    q.ntok = tok->ntok;
+    q.x_st = tok->x_stride_t; q.dt_st = tok->dt_stride_t; q.B_st = tok->B_stride_t;
+    q.C_st = tok->C_stride_t; q.out_st = tok->out_stride_t;
+  }
+  fill_pool(pool, sp);
+  fill_inputs(a, sp);
+  return NSSM_OK;
+}
+
+// R rotation of the ntok tokens' B and C (token-contiguous rows) into the workspace.
+int spec_rotate(const nssm_step_args* a, int ntok, int G, int N, nssm::StepParams& sp, nssm::SpecParams& q,
+                cudaStream_t st) {
+  sp.B = a->B; sp.B_sb = a->B_stride_b;
+  sp.C = a->C; sp.C_sb = a->C_stride_b;
+  if (!a->R) return NSSM_OK;
+  if (N != 128) return fail(NSSM_ERR_UNSUPPORTED, "rotation compiled for dstate 128 only");
+  if (reinterpret_cast<uintptr_t>(a->R) % 16) return fail(NSSM_ERR_INVALID, "R must be 16-byte aligned");
+  if (ntok > 1 && (a->B_stride_b != ntok * q.B_st || a->C_stride_b != ntok * q.C_st))
+    return fail(NSSM_ERR_INVALID, "with R, B and C rows must be token-contiguous (stride_b == ntok * stride_t)");
+  const int rows = a->batch * ntok;
+  const size_t half = nssm_step_workspace_bytes(rows, G, N, a->io_dtype, 1) / 2;
+  nssm::RotParams rp{};
+  rp.x0 = a->B; rp.xs0 = ntok > 1 ? q.B_st : a->B_stride_b;
+  rp.x1 = a->C; rp.xs1 = ntok > 1 ? q.C_st : a->C_stride_b;
+  rp.o0 = a->workspace; rp.os0 = (int64_t)G * N;
+  rp.o1 = static_cast<char*>(a->workspace) + half; rp.os1 = (int64_t)G * N;
+  rp.R = a->R; rp.T = rows; rp.G = G; rp.dtype = a->io_dtype;
+  int rc = launch_rot(rp, 2 * rows, G, st);
+  if (rc) return rc;
+  sp.B = rp.o0; sp.B_sb = (int64_t)ntok * G * N; q.B_st = (int64_t)G * N;
+  sp.C = rp.o1; sp.C_sb = (int64_t)ntok * G * N; q.C_st = (int64_t)G * N;
+  return NSSM_OK;
+}
+
 }  // namespace
 
 extern "C" {
+
+size_t nssm_spec_workspace_bytes(int32_t batch, int32_t ntok, int32_t ngroups, int32_t dstate, int32_t io_dtype,
+                                 int32_t has_rotation) {
+  if (batch <= 0 || ntok <= 0) return 0;
+  const size_t rot = nssm_step_workspace_bytes(batch * ntok, ngroups, dstate, io_dtype, has_rotation);
+  return rot + ((size_t)batch * 4 + 255) / 256 * 256;
+}
+
+int nssm_draft_step(const nssm_pool* pool, float* draft, int32_t from_pool, const nssm_step_args* args,
+                    void* stream) {
+  nssm::StepParams sp{};
+  nssm::SpecParams q{};
+  int rc = spec_prepare(pool, args, nullptr, sp, q);
+  if (rc) return rc;
+  if (!draft || !aligned16(draft)) return fail(NSSM_ERR_INVALID, "draft must be a 16-byte aligned device pointer");
+  if (args->batch == 0) return NSSM_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (args->R) {
+    const size_t need = nssm_step_workspace_bytes(args->batch, pool->ngroups, pool->dstate, args->io_dtype, 1);
+    if (!args->workspace || args->workspace_bytes < need)
+      return fail(NSSM_ERR_INVALID, "workspace of %zu bytes needed for the rotation (got %zu)", need,
+                  args->workspace_bytes);
+  }
+  rc = spec_rotate(args, 1, pool->ngroups, pool->dstate, sp, q, st);
+  if (rc) return rc;
+  q.sp = sp;
+  q.ntok = 1;
+  q.draft = draft;
+  q.from_pool = from_pool ? 1 : 0;
+  return dispatch(OP_DRAFT, pool->dstate, pool->hot_dim, pool->cold_dtype, &q, args->batch, st);
+}
+
+int nssm_verify_step(const nssm_pool* pool, const nssm_step_args* args, const nssm_token_args* tok, void* stream) {
+  if (!tok) return fail(NSSM_ERR_INVALID, "tok is NULL");
+  nssm::StepParams sp{};
+  nssm::SpecParams q{};
+  int rc = spec_prepare(pool, args, tok, sp, q);
+  if (rc) return rc;
+  if (args->mode == NSSM_MODE_CORR) return fail(NSSM_ERR_UNSUPPORTED, "verify reads modes STALE and COLDOFF");
+  if (args->batch == 0) return NSSM_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (args->R) {
+    const size_t need = nssm_spec_workspace_bytes(args->batch, tok->ntok, pool->ngroups, pool->dstate, args->io_dtype, 1);
+    if (!args->workspace || args->workspace_bytes < need)
+      return fail(NSSM_ERR_INVALID, "workspace of %zu bytes needed (got %zu)", need, args->workspace_bytes);
+  }
+  rc = spec_rotate(args, tok->ntok, pool->ngroups, pool->dstate, sp, q, st);
+  if (rc) return rc;
+  q.sp = sp;
+  return dispatch(OP_VERIFY, pool->dstate, pool->hot_dim, pool->cold_dtype, &q, args->batch, st);
+}
+
+int nssm_commit_step(const nssm_pool* pool, const nssm_step_args* args, const nssm_token_args* tok, void* stream) {
+  if (!tok) return fail(NSSM_ERR_INVALID, "tok is NULL");
+  if (!tok->accept) return fail(NSSM_ERR_INVALID, "tok->accept is NULL");
+  nssm::StepParams sp{};
+  nssm::SpecParams q{};
+  int rc = spec_prepare(pool, args, tok, sp, q);
+  if (rc) return rc;
+  if (args->batch == 0) return NSSM_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t need = nssm_spec_workspace_bytes(args->batch, tok->ntok, pool->ngroups, pool->dstate, args->io_dtype,
+                                                args->R ? 1 : 0);
+  if (!args->workspace || args->workspace_bytes < need || !aligned16(args->workspace))
+    return fail(NSSM_ERR_INVALID, "a 16-byte aligned workspace of %zu bytes is needed (got %zu)", need,
+                args->workspace_bytes);
+  rc = spec_rotate(args, tok->ntok, pool->ngroups, pool->dstate, sp, q, st);
+  if (rc) return rc;
+  q.sp = sp;
+  q.accept = tok->accept;
+  q.flush_idx = reinterpret_cast<int32_t*>(
+      static_cast<char*>(args->workspace) +
+      nssm_step_workspace_bytes(args->batch * tok->ntok, pool->ngroups, pool->dstate, args->io_dtype, args->R ? 1 : 0));
+  return dispatch(OP_COMMIT, pool->dstate, pool->hot_dim, pool->cold_dtype, &q, args->batch, st);
+}
 
 size_t nssm_step_workspace_bytes(int32_t batch, int32_t ngroups, int32_t dstate, int32_t io_dtype,
                                  int32_t has_rotation) {
@@ -491,6 +622,7 @@ int32_t nssm_test_inject_stuck_copy(int32_t enable) {
 
 size_t nssm_sizeof_pool(void) { return sizeof(nssm_pool); }
 size_t nssm_sizeof_step_args(void) { return sizeof(nssm_step_args); }
+size_t nssm_sizeof_token_args(void) { return sizeof(nssm_token_args); }
 int32_t nssm_abi_version(void) { return NSSM_ABI_VERSION; }
 const char* nssm_last_error(void) { return g_last_error.c_str(); }
 

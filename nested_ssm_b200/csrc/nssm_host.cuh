@@ -13,6 +13,7 @@
 
 #include "nssm_persistent.cuh"
 #include "nssm_flush_mma.cuh"
+#include "nssm_spec.cuh"
 #include "nssm_rot.cuh"
 #include "nssm_conv.cuh"
 
@@ -142,27 +143,13 @@ inline int launch_flush_mma(const nssm::StepParams& sp, int batch, cudaStream_t 
   return NSSM_OK;
 }
 
-// Both phases of one step.  The production configuration (fp8 cold, bf16 io) has
-// instances compiled for c in {4, 8, 16, 64} and headdim in {64, 80}; anything else
-// runs the instances that read c and headdim at run time.  Its FLUSH is the tensor-core
-// kernel (NSSM_LEGACY_FLUSH builds keep the banded FLUSH phase of the persistent kernel).
+// The FLUSH of the rows whose t is a multiple of c (after their STEP or commit).  The
+// production configuration's is the tensor-core kernel (NSSM_LEGACY_FLUSH builds keep the
+// banded FLUSH phase of the persistent kernel).
 template <int PB, int NC, int COLD, bool IOBF, int CFIX, int RPWC>
-inline int launch_both(const nssm::StepParams& sp, int batch, cudaStream_t st, bool ring_ok, int sms) {
+inline int launch_flush_part(const nssm::StepParams& sp, int batch, cudaStream_t st, bool ring_ok, int sms) {
   bool done = false;
   int rc = NSSM_OK;
-  // the fused norm runs in the production instances' STEP; elsewhere the step writes y and
-  // the caller of the dispatch applies the norm kernel (g_norm_fused stays false)
-  constexpr bool kNormable = COLD == nssm::COLD_FP8 && IOBF && RPWC > 0;
-  if constexpr (kNormable) {
-    if (sp.ngate) {
-      rc = launch_phase<PB, NC, COLD, IOBF, nssm::PH_STEP, CFIX, RPWC, true>(sp, batch, st, ring_ok, sms, &done);
-      if (rc) return rc;
-      g_norm_fused = done;
-    }
-  }
-  if (!done) rc = launch_phase<PB, NC, COLD, IOBF, nssm::PH_STEP, CFIX, RPWC>(sp, batch, st, ring_ok, sms, &done);
-  if (rc) return rc;
-  if (!done) return launch_step<PB, NC, COLD, kTPR>(sp, batch, st);
   if constexpr (COLD == nssm::COLD_FP8 && IOBF && (CFIX == 4 || CFIX == 8 || CFIX == 16 || CFIX == 64) &&
                 (RPWC == 8 || RPWC == 10) && NC % 16 == 0) {
 #ifndef NSSM_LEGACY_FLUSH
@@ -179,50 +166,131 @@ inline int launch_both(const nssm::StepParams& sp, int batch, cudaStream_t st, b
   return NSSM_OK;
 }
 
-template <int PB, int NC, int COLD, bool IOBF, int RPWC>
-inline int launch_c(const nssm::StepParams& sp, int batch, cudaStream_t st, bool ring_ok, int sms) {
-  switch (sp.c) {
-    case 4: return launch_both<PB, NC, COLD, IOBF, 4, RPWC>(sp, batch, st, ring_ok, sms);
-    case 8: return launch_both<PB, NC, COLD, IOBF, 8, RPWC>(sp, batch, st, ring_ok, sms);
-    case 16: return launch_both<PB, NC, COLD, IOBF, 16, RPWC>(sp, batch, st, ring_ok, sms);
-    case 64: return launch_both<PB, NC, COLD, IOBF, 64, RPWC>(sp, batch, st, ring_ok, sms);
+// Both phases of one step (FLUSH_ONLY: the FLUSH alone, after a commit).  The production
+// configuration (fp8 cold, bf16 io) has instances compiled for c in {4, 8, 16, 64} and
+// headdim in {64, 80}; anything else runs the instances that read c and headdim at run time.
+template <int PB, int NC, int COLD, bool IOBF, int CFIX, int RPWC, bool FLUSH_ONLY = false>
+inline int launch_both(const nssm::StepParams& sp, int batch, cudaStream_t st, bool ring_ok, int sms) {
+  if constexpr (FLUSH_ONLY) return launch_flush_part<PB, NC, COLD, IOBF, CFIX, RPWC>(sp, batch, st, ring_ok, sms);
+  bool done = false;
+  int rc = NSSM_OK;
+  // the fused norm runs in the production instances' STEP; elsewhere the step writes y and
+  // the caller of the dispatch applies the norm kernel (g_norm_fused stays false)
+  constexpr bool kNormable = COLD == nssm::COLD_FP8 && IOBF && RPWC > 0;
+  if constexpr (kNormable) {
+    if (sp.ngate) {
+      rc = launch_phase<PB, NC, COLD, IOBF, nssm::PH_STEP, CFIX, RPWC, true>(sp, batch, st, ring_ok, sms, &done);
+      if (rc) return rc;
+      g_norm_fused = done;
+    }
   }
-  return launch_both<PB, NC, COLD, IOBF, 0, 0>(sp, batch, st, ring_ok, sms);
+  if (!done) rc = launch_phase<PB, NC, COLD, IOBF, nssm::PH_STEP, CFIX, RPWC>(sp, batch, st, ring_ok, sms, &done);
+  if (rc) return rc;
+  if (!done) return launch_step<PB, NC, COLD, kTPR>(sp, batch, st);
+  return launch_flush_part<PB, NC, COLD, IOBF, CFIX, RPWC>(sp, batch, st, ring_ok, sms);
 }
 
-template <int PB, int NC, int COLD, bool IOBF>
+template <int PB, int NC, int COLD, bool IOBF, int RPWC, bool FLUSH_ONLY>
+inline int launch_c(const nssm::StepParams& sp, int batch, cudaStream_t st, bool ring_ok, int sms) {
+  switch (sp.c) {
+    case 4: return launch_both<PB, NC, COLD, IOBF, 4, RPWC, FLUSH_ONLY>(sp, batch, st, ring_ok, sms);
+    case 8: return launch_both<PB, NC, COLD, IOBF, 8, RPWC, FLUSH_ONLY>(sp, batch, st, ring_ok, sms);
+    case 16: return launch_both<PB, NC, COLD, IOBF, 16, RPWC, FLUSH_ONLY>(sp, batch, st, ring_ok, sms);
+    case 64: return launch_both<PB, NC, COLD, IOBF, 64, RPWC, FLUSH_ONLY>(sp, batch, st, ring_ok, sms);
+  }
+  return launch_both<PB, NC, COLD, IOBF, 0, 0, FLUSH_ONLY>(sp, batch, st, ring_ok, sms);
+}
+
+template <int PB, int NC, int COLD, bool IOBF, bool FLUSH_ONLY = false>
 inline int launch_persistent(const nssm::StepParams& sp, int batch, cudaStream_t st, bool ring_ok) {
   const long long items = (long long)batch * sp.H;
-  if (items > (1ll << 30)) return launch_step<PB, NC, COLD, kTPR>(sp, batch, st);
+  if (items > (1ll << 30)) {
+    if constexpr (FLUSH_ONLY) return fail(NSSM_ERR_UNSUPPORTED, "batch too large for the persistent FLUSH");
+    return launch_step<PB, NC, COLD, kTPR>(sp, batch, st);
+  }
   int sms = 0;
   int rc = sm_count(&sms);
   if (rc) return rc;
   if constexpr (COLD == nssm::COLD_FP8 && IOBF) {
-    if (sp.P == 80) return launch_c<PB, NC, COLD, IOBF, 10>(sp, batch, st, ring_ok, sms);
-    if (sp.P == 64) return launch_c<PB, NC, COLD, IOBF, 8>(sp, batch, st, ring_ok, sms);
+    if (sp.P == 80) return launch_c<PB, NC, COLD, IOBF, 10, FLUSH_ONLY>(sp, batch, st, ring_ok, sms);
+    if (sp.P == 64) return launch_c<PB, NC, COLD, IOBF, 8, FLUSH_ONLY>(sp, batch, st, ring_ok, sms);
   }
-  return launch_both<PB, NC, COLD, IOBF, 0, 0>(sp, batch, st, ring_ok, sms);
+  return launch_both<PB, NC, COLD, IOBF, 0, 0, FLUSH_ONLY>(sp, batch, st, ring_ok, sms);
 }
 
+// Whether the persistent TMA-pipelined kernels take this call (else the simple kernel runs):
+// 16-byte aligned pool tiles and input rows, headdim % 4 == 0 and <= kPMaxPersistent.
 template <int PB, int NC, int COLD>
-inline int launch_tiered(const nssm::StepParams& sp, int batch, cudaStream_t st) {
+inline bool persistent_ok(const nssm::StepParams& sp, bool* ring_ok) {
   constexpr int N = PB + NC;
   const int iob = io_bytes(sp.io_dtype);
-#ifdef NSSM_FORCE_SIMPLE
-  return launch_step<PB, NC, COLD, kTPR>(sp, batch, st);
-#endif
   auto a16 = [](long long v) { return (v % 16) == 0; };
   const bool tma_ok = sp.P % 4 == 0 && sp.P <= nssm::kPMaxPersistent && aligned16(sp.hot) &&
                       aligned16(sp.cold) && (COLD != COLD_FP8 || aligned16(sp.scale)) && aligned16(sp.x) &&
                       a16(sp.x_sb * iob) && a16(sp.x_sh * iob) && a16((long long)sp.P * iob) &&
                       aligned16(sp.B) && aligned16(sp.C) && a16(sp.B_sb * iob) && a16(sp.C_sb * iob) &&
                       a16((long long)N * iob);
-  if (!tma_ok) return launch_step<PB, NC, COLD, kTPR>(sp, batch, st);
-  const bool ring_ok = sp.c <= nssm::kRingInStage && aligned16(sp.ring_x) && aligned16(sp.ring_b) &&
-                       aligned16(sp.ring_dt) && a16((long long)sp.c * sp.P * iob) &&
-                       a16((long long)sp.c * NC * 4);
+  *ring_ok = sp.c <= nssm::kRingInStage && aligned16(sp.ring_x) && aligned16(sp.ring_b) &&
+             aligned16(sp.ring_dt) && a16((long long)sp.c * sp.P * iob) && a16((long long)sp.c * NC * 4);
+  return tma_ok;
+}
+
+template <int PB, int NC, int COLD>
+inline int launch_tiered(const nssm::StepParams& sp, int batch, cudaStream_t st) {
+#ifdef NSSM_FORCE_SIMPLE
+  return launch_step<PB, NC, COLD, kTPR>(sp, batch, st);
+#endif
+  bool ring_ok = false;
+  if (!persistent_ok<PB, NC, COLD>(sp, &ring_ok)) return launch_step<PB, NC, COLD, kTPR>(sp, batch, st);
   if (sp.io_dtype == NSSM_BF16) return launch_persistent<PB, NC, COLD, true>(sp, batch, st, ring_ok);
   return launch_persistent<PB, NC, COLD, false>(sp, batch, st, ring_ok);
+}
+
+// ---- self-speculative decoding ---------------------------------------------
+template <int PB, int NC>
+int launch_draft(const nssm::SpecParams& q, int batch, cudaStream_t st) {
+  dim3 grid(q.sp.H, batch);
+  const int threads = round_up(q.sp.P * kTPR, 32);
+  nssm::draft_step_kernel<PB, PB + NC, kTPR><<<grid, threads, 0, st>>>(q);
+  return cuda_check("draft_step_kernel launch");
+}
+
+// The commit's FLUSH runs on the persistent kernels only; verify and commit refuse a call
+// those kernels cannot take before launching anything.
+template <int PB, int NC, int COLD>
+int launch_verify(const nssm::SpecParams& q, int batch, cudaStream_t st) {
+  bool ring_ok = false;
+  if (!persistent_ok<PB, NC, COLD>(q.sp, &ring_ok))
+    return fail(NSSM_ERR_UNSUPPORTED, "verify / commit need the persistent kernels' layout (16-byte aligned rows, "
+                                      "headdim %% 4 == 0 and <= %d)", nssm::kPMaxPersistent);
+  dim3 grid(q.sp.H, batch);
+  const int threads = round_up(q.sp.P * kTPR, 32);
+  const size_t smem = sizeof(float) * nssm::verify_smem_floats<PB, NC, COLD>(q.sp.P);
+  auto fn = nssm::verify_step_kernel<PB, NC, COLD, kTPR>;
+  if (smem > 48 * 1024) {
+    int rc = ensure_smem_attr(reinterpret_cast<const void*>(fn));
+    if (rc) return rc;
+  }
+  fn<<<grid, threads, smem, st>>>(q);
+  return cuda_check("verify_step_kernel launch");
+}
+
+template <int PB, int NC, int COLD>
+int launch_commit(const nssm::SpecParams& q, int batch, cudaStream_t st) {
+  bool ring_ok = false;
+  if (!persistent_ok<PB, NC, COLD>(q.sp, &ring_ok))
+    return fail(NSSM_ERR_UNSUPPORTED, "verify / commit need the persistent kernels' layout (16-byte aligned rows, "
+                                      "headdim %% 4 == 0 and <= %d)", nssm::kPMaxPersistent);
+  dim3 grid(q.sp.H, batch);
+  const int threads = round_up(q.sp.P * kTPR, 32);
+  nssm::commit_step_kernel<PB, PB + NC, kTPR><<<grid, threads, 0, st>>>(q);
+  int rc = cuda_check("commit_step_kernel launch");
+  if (rc) return rc;
+  nssm::StepParams fs = q.sp;   // FLUSH of the rows the commit completed (the others are -1)
+  fs.idx = q.flush_idx;
+  fs.pad = -1;
+  if (fs.io_dtype == NSSM_BF16) return launch_persistent<PB, NC, COLD, true, true>(fs, batch, st, ring_ok);
+  return launch_persistent<PB, NC, COLD, false, true>(fs, batch, st, ring_ok);
 }
 
 template <int PB, int NC, int COLD, int TPR>
@@ -242,7 +310,7 @@ int launch_mat(const nssm::MatParams& mp, int batch, cudaStream_t st) {
 }
 
 // Instances compiled: dstate 128, hot width 16/32/64, cold fp8/bf16/fp32.
-enum Op { OP_STEP, OP_SPLIT, OP_MAT };
+enum Op { OP_STEP, OP_SPLIT, OP_MAT, OP_DRAFT, OP_VERIFY, OP_COMMIT };
 
 template <int PB, int COLD>
 int run_op(Op op, const void* params, int batch, cudaStream_t st) {
@@ -251,6 +319,9 @@ int run_op(Op op, const void* params, int batch, cudaStream_t st) {
     case OP_STEP: return launch_tiered<PB, NC, COLD>(*static_cast<const nssm::StepParams*>(params), batch, st);
     case OP_SPLIT: return launch_split<PB, NC, COLD, kTPR>(*static_cast<const nssm::SplitParams*>(params), batch, st);
     case OP_MAT: return launch_mat<PB, NC, COLD, kTPR>(*static_cast<const nssm::MatParams*>(params), batch, st);
+    case OP_DRAFT: return launch_draft<PB, NC>(*static_cast<const nssm::SpecParams*>(params), batch, st);
+    case OP_VERIFY: return launch_verify<PB, NC, COLD>(*static_cast<const nssm::SpecParams*>(params), batch, st);
+    case OP_COMMIT: return launch_commit<PB, NC, COLD>(*static_cast<const nssm::SpecParams*>(params), batch, st);
   }
   return fail(NSSM_ERR_INVALID, "unknown op");
 }

@@ -1,0 +1,429 @@
+// Self-speculative decoding on the tiered state: the hot-only draft step, the multi-token
+// verify and the commit of the accepted tokens.
+//
+//   draft  (draft_step_kernel): one token of the hot-only model -- h <- h exp(dt A) +
+//          (dt B_hot) x on a separate [S][H][P][pb] fp32 draft state (read from the pool's
+//          hot slice on the first draft token), y = C_hot . h + D x; the pool is not touched.
+//          The reference's cold="off" install (scale/v4_fused_decode.py:49-55 on the hot slice,
+//          :140-142 no cold at all).
+//   verify (verify_step_kernel): y of n tokens per row read against the committed tiered state
+//          exactly as n successive decode tokens would read it (hot updated token by token in
+//          registers, the stale cold slice read once, exp(glog) advanced by each token's dt A).
+//          Read-only on the pool.  The window may end on a chunk boundary but not cross it:
+//          (t % c) + n <= c.
+//   commit (commit_step_kernel): the first k of those tokens made permanent -- the hot slice
+//          replayed over them, their (x, dt, B_cold) written to the ring at t%c .. t%c+k-1,
+//          glog and t advanced, and every row whose chunk is now complete named in flush_idx
+//          for the FLUSH kernels that follow.  Commit of k tokens leaves the pool exactly as k
+//          decode steps would (same arithmetic, same operation order).
+#pragma once
+
+#include "nssm_device.cuh"
+
+namespace nssm {
+
+enum : int { STATUS_SPEC_WINDOW = 4 };   // a window crosses a chunk boundary, or accept is out of range
+
+struct SpecParams {
+  StepParams sp;               // pool, per-row / per-head strides, token 0 of every input
+  int ntok;                    // tokens per row in this call
+  int64_t x_st, dt_st, B_st, C_st, out_st;   // element strides between a row's tokens
+  const int32_t* accept;       // commit: tokens kept per batch row, 0..ntok
+  int32_t* flush_idx;          // commit: slot of each row whose chunk completed, else -1
+  float* draft;                // draft: [S][H][P][PB] fp32 draft state
+  int from_pool;               // draft: read the pool's hot slice instead of the draft state
+};
+
+// dt of one (row, head, token): softplus(dt + dt_bias), clamped below, as the decode step
+__device__ __forceinline__ float spec_dt(const StepParams& p, int b, int h, int64_t toff) {
+  float d = ld_io(p.dt, (int64_t)b * p.dt_sb + (int64_t)h * p.dt_sh + toff, p.dt_dtype);
+  if (p.dt_bias) d += p.dt_bias[h];
+  if (p.softplus) d = softplus_f(d);
+  if (p.dt_min > 0.0f) d = fmaxf(d, p.dt_min);
+  return d;
+}
+
+// h <- h exp(dt A) + (dt B) x on the thread's hot chunks, and the row sums C . h into yh.
+// Chunk i = k*T + tid holds hot[i / LPR][4 (i % LPR) ..]; the LPR lanes of a row are
+// consecutive lanes of one warp (T % LPR == 0).
+template <int PB, int HCH>
+__device__ __forceinline__ void hot_token(float4 (&hv)[HCH], int T, int tid, int nh, float dt, float decay,
+                                          const float* Bs, const float* Cs, const float* s_x, float* yh,
+                                          bool sums) {
+  constexpr int LPR = PB / 4;
+  const int hcol = tid % LPR;
+  float dtB[4], ch[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    dtB[e] = dt * Bs[hcol * 4 + e];
+    ch[e] = Cs ? Cs[hcol * 4 + e] : 0.0f;
+  }
+#pragma unroll
+  for (int k = 0; k < HCH; ++k) {
+    const int i = k * T + tid;
+    float part = 0.0f;
+    if (i < nh) {
+      const float xp = s_x[i / LPR];
+      float4 v = hv[k];
+      v.x = fmaf(v.x, decay, dtB[0] * xp);
+      v.y = fmaf(v.y, decay, dtB[1] * xp);
+      v.z = fmaf(v.z, decay, dtB[2] * xp);
+      v.w = fmaf(v.w, decay, dtB[3] * xp);
+      hv[k] = v;
+      part = fmaf(v.x, ch[0], fmaf(v.y, ch[1], fmaf(v.z, ch[2], v.w * ch[3])));
+    }
+    if (sums) {
+#pragma unroll
+      for (int o = 1; o < LPR; o <<= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+      if (hcol == 0 && i < nh) yh[i / LPR] = part;
+    }
+  }
+}
+
+// ---- draft ------------------------------------------------------------------
+template <int PB, int N, int TPR>
+__global__ void __launch_bounds__(128 * TPR) draft_step_kernel(const SpecParams q) {
+  const StepParams& p = q.sp;
+  constexpr int LPR = PB / 4;
+  constexpr int HCH = (LPR + TPR - 1) / TPR;
+  const int T = blockDim.x, tid = threadIdx.x;
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int Pn = p.P;
+  __shared__ float Bs[PB], Cs[PB], s_x[128], yh[128];
+  __shared__ float s_dt, s_decay;
+
+  const int slot = p.idx ? p.idx[b] : b;
+  if (slot == p.pad) return;
+  if (slot < 0 || slot >= p.S) {
+    if (tid == 0 && p.status) atomicOr(p.status, STATUS_BAD_SLOT);
+    return;
+  }
+  const int g = h / (p.H / p.G);
+  const int64_t sh = (int64_t)slot * p.H + h;
+  const float4* src = reinterpret_cast<const float4*>((q.from_pool ? p.hot : q.draft) + sh * (int64_t)Pn * PB);
+  float4* dst = reinterpret_cast<float4*>(q.draft + sh * (int64_t)Pn * PB);
+  const int nh = Pn * LPR;
+  float4 hv[HCH];
+#pragma unroll
+  for (int k = 0; k < HCH; ++k) {
+    const int i = k * T + tid;
+    if (i < nh) hv[k] = src[i];
+  }
+  if (tid < Pn) s_x[tid] = ld_io(p.x, (int64_t)b * p.x_sb + (int64_t)h * p.x_sh + tid, p.io_dtype);
+  for (int n = tid; n < PB; n += T) {
+    Bs[n] = ld_io(p.B, (int64_t)b * p.B_sb + (int64_t)g * N + n, p.io_dtype);
+    Cs[n] = ld_io(p.C, (int64_t)b * p.C_sb + (int64_t)g * N + n, p.io_dtype);
+  }
+  if (tid == 0) {
+    const float d = spec_dt(p, b, h, 0);
+    s_dt = d;
+    s_decay = expf(d * p.A[h]);
+  }
+  __syncthreads();
+  hot_token<PB, HCH>(hv, T, tid, nh, s_dt, s_decay, Bs, Cs, s_x, yh, true);
+#pragma unroll
+  for (int k = 0; k < HCH; ++k) {
+    const int i = k * T + tid;
+    if (i < nh) dst[i] = hv[k];
+  }
+  __syncthreads();
+  if (tid < Pn) {
+    float y = yh[tid];
+    if (p.D) y = fmaf(s_x[tid], p.D[h], y);
+    st_io(p.out, (int64_t)b * p.out_sb + (int64_t)h * p.out_sh + tid, p.out_dtype, y);
+  }
+}
+
+// ---- verify -----------------------------------------------------------------
+// Tokens are taken TC at a time: their x, B_hot, C and dt scalars are staged with one round of
+// loads (the item's cold rows are loaded in the same round), the cold partials of every staged
+// token are formed from the cold chunks decoded once, the hot recurrence runs through the
+// tokens in registers, and one pass writes their y -- two block barriers per TC tokens.
+// C_cold is staged in chunks of CE values at a padded stride CS, so the 128-bit shared reads
+// of any 8 consecutive threads (one quarter-warp) fall in distinct banks.
+template <int COLD> struct VerifyTC { static constexpr int kV = COLD == COLD_F32 ? 4 : 8; };
+
+template <int PB, int NC, int COLD>
+struct VerifyShape {
+  using Sh = StepShape<PB, NC, COLD>;
+  static constexpr int TC = VerifyTC<COLD>::kV;
+  static constexpr int CS = Sh::CE == 4 ? 4 : Sh::CE + 4;   // padded chunk stride (floats)
+  static constexpr int CW = Sh::CPR * CS;                    // C_cold floats per token
+  // dynamic shared floats: per staged token Bh, Ch [PB], Cc [CW], s_x, yh [P], pc [P * CPR];
+  // s_sco [P]; per staged token dt, dA, exp(dA), exp(glog) [4 * TC]
+  __host__ __device__ static constexpr size_t smem_floats(int P) {
+    return (size_t)TC * (2 * PB + CW + 2 * (size_t)P + (size_t)P * Sh::CPR) + (size_t)P + 4 * (size_t)TC;
+  }
+};
+
+template <int PB, int NC, int COLD>
+__host__ __device__ constexpr size_t verify_smem_floats(int P) {
+  return VerifyShape<PB, NC, COLD>::smem_floats(P);
+}
+
+template <int PB, int NC, int COLD, int TPR>
+__global__ void __launch_bounds__(128 * TPR, COLD == COLD_FP8 ? 3 : 2) verify_step_kernel(const SpecParams q) {
+  const StepParams& p = q.sp;
+  using Sh = StepShape<PB, NC, COLD>;
+  using VS = VerifyShape<PB, NC, COLD>;
+  constexpr int N = Sh::N;
+  constexpr int LPR = Sh::LPR;
+  constexpr int CPR = Sh::CPR;
+  constexpr int CE = Sh::CE;
+  constexpr int CS = VS::CS;
+  constexpr int CW = VS::CW;
+  constexpr int HCH = (LPR + TPR - 1) / TPR;
+  constexpr int KCH = (CPR + TPR - 1) / TPR;
+  constexpr int kPerW = WordTraits<COLD>::kPer;
+  constexpr int TC = VS::TC;
+  static_assert(Sh::kCold, "tiered instances only");
+  static_assert(CE % 4 == 0, "cold chunks are whole float4s");
+
+  const int T = blockDim.x, tid = threadIdx.x;
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int Pn = p.P, c = p.c;
+  const int ncc = Pn * CPR;
+  extern __shared__ __align__(16) float smem[];
+  float* Bh = smem;                 // [TC][PB]
+  float* Ch = Bh + TC * PB;         // [TC][PB]
+  float* Cc = Ch + TC * PB;         // [TC][CW]   C_cold, chunk m at m * CS
+  float* s_x = Cc + TC * CW;        // [TC][P]
+  float* yh = s_x + TC * Pn;        // [TC][P]
+  float* pc = yh + TC * Pn;         // [TC][P * CPR]
+  float* s_sco = pc + TC * ncc;     // [P]
+  float* s_dt = s_sco + Pn;         // [TC]
+  float* s_dA = s_dt + TC;          // [TC]
+  float* s_dec = s_dA + TC;         // [TC]
+  float* s_eg = s_dec + TC;         // [TC]
+  __shared__ int s_r;
+
+  const int slot = p.idx ? p.idx[b] : b;
+  if (slot == p.pad) return;
+  if (slot < 0 || slot >= p.S) {
+    if (tid == 0 && p.status) atomicOr(p.status, STATUS_BAD_SLOT);
+    return;
+  }
+  const int g = h / (p.H / p.G);
+  const int64_t sh = (int64_t)slot * p.H + h;
+
+  const int nh = Pn * LPR;
+  const float4* hot4 = reinterpret_cast<const float4*>(p.hot + sh * (int64_t)Pn * PB);
+  float4 hv[HCH];
+#pragma unroll
+  for (int k = 0; k < HCH; ++k) {
+    const int i = k * T + tid;
+    if (i < nh) hv[k] = hot4[i];
+  }
+  if (tid < Pn) s_sco[tid] = (COLD == COLD_FP8) ? p.scale[sh * Pn + tid] : 1.0f;
+  float glog = 0.0f;   // thread 0: glog before the next token to be read
+  if (tid == 0) {
+    const int r = p.t[sh] % c;
+    s_r = (r + q.ntok <= c) ? r : -1;
+    glog = p.glog[sh];
+  }
+  __syncthreads();
+  if (s_r < 0) {
+    if (tid == 0 && p.status) atomicOr(p.status, STATUS_SPEC_WINDOW);
+    return;
+  }
+  const float A_h = p.A[h];
+  const float Dh = p.D ? p.D[h] : 0.0f;
+  const bool cold_read = p.mode != NSSM_MODE_COLDOFF;
+  const uint4* cold16 = reinterpret_cast<const uint4*>(static_cast<const char*>(p.cold) + sh * (int64_t)Pn * NC * Sh::ESZ);
+
+  for (int j0 = 0; j0 < q.ntok; j0 += TC) {
+    const int nt = min(TC, q.ntok - j0);
+    // ---- one round of loads: the staged tokens' inputs and the item's cold rows
+    uint4 cw[KCH];
+    if (cold_read) {
+#pragma unroll
+      for (int k = 0; k < KCH; ++k) {
+        const int i = k * T + tid;
+        if (i < ncc) cw[k] = cold16[i];
+      }
+    }
+    for (int e = tid; e < nt * Pn; e += T) {
+      const int j = e / Pn, r = e - j * Pn;
+      s_x[e] = ld_io(p.x, (int64_t)b * p.x_sb + (j0 + j) * q.x_st + (int64_t)h * p.x_sh + r, p.io_dtype);
+    }
+    for (int e = tid; e < nt * N; e += T) {
+      const int j = e / N, n = e - j * N;
+      const int64_t row = (int64_t)(j0 + j);
+      if (n < PB) {
+        Bh[j * PB + n] = ld_io(p.B, (int64_t)b * p.B_sb + row * q.B_st + (int64_t)g * N + n, p.io_dtype);
+        Ch[j * PB + n] = ld_io(p.C, (int64_t)b * p.C_sb + row * q.C_st + (int64_t)g * N + n, p.io_dtype);
+      } else if (cold_read) {
+        const int m = (n - PB) / CE, u = (n - PB) - m * CE;
+        Cc[j * CW + m * CS + u] = ld_io(p.C, (int64_t)b * p.C_sb + row * q.C_st + (int64_t)g * N + n, p.io_dtype);
+      }
+    }
+    if (tid < nt) {
+      const float d = spec_dt(p, b, h, (j0 + tid) * q.dt_st);
+      const float dA = d * A_h;
+      s_dt[tid] = d;
+      s_dA[tid] = dA;
+      s_dec[tid] = expf(dA);
+    }
+    __syncthreads();
+    if (tid == 0) {   // the stale read of token j: glog + dA_0 + ... + dA_{j-1}, summed in token order
+      for (int j = 0; j < nt; ++j) {
+        s_eg[j] = expf(glog);
+        glog = glog + s_dA[j];
+      }
+    }
+    // ---- cold partials of every staged token from the chunks decoded once
+    if (cold_read) {
+#pragma unroll
+      for (int k = 0; k < KCH; ++k) {
+        const int i = k * T + tid;
+        if (i < ncc) {
+          const uint32_t wv[4] = {cw[k].x, cw[k].y, cw[k].z, cw[k].w};
+          float qv[CE];
+#pragma unroll
+          for (int wi = 0; wi < 4; ++wi) word_to_float<COLD>(wv[wi], qv + wi * kPerW);
+          const int coff = (i % CPR) * CS;
+          for (int j = 0; j < nt; ++j) {
+            const float4* c4 = reinterpret_cast<const float4*>(Cc + j * CW + coff);
+            float part = 0.0f;
+#pragma unroll
+            for (int v = 0; v < CE / 4; ++v) {
+              const float4 cv = c4[v];
+              part = fmaf(qv[4 * v], cv.x, part);
+              part = fmaf(qv[4 * v + 1], cv.y, part);
+              part = fmaf(qv[4 * v + 2], cv.z, part);
+              part = fmaf(qv[4 * v + 3], cv.w, part);
+            }
+            pc[j * ncc + i] = part;
+          }
+        }
+      }
+    }
+    // ---- the hot recurrence through the staged tokens, row sums per token
+    for (int j = 0; j < nt; ++j)
+      hot_token<PB, HCH>(hv, T, tid, nh, s_dt[j], s_dec[j], Bh + j * PB, Ch + j * PB, s_x + j * Pn, yh + j * Pn,
+                         true);
+    __syncthreads();
+    // ---- y of every (token, row)
+    for (int e = tid; e < nt * Pn; e += T) {
+      const int j = e / Pn, row = e - j * Pn;
+      float y = yh[e];
+      if (cold_read) {
+        float yc = 0.0f;
+#pragma unroll
+        for (int cc = 0; cc < CPR; ++cc) yc += pc[j * ncc + row * CPR + cc];
+        y += (yc * s_sco[row]) * s_eg[j];
+      }
+      if (p.D) y = fmaf(s_x[e], Dh, y);
+      st_io(p.out, (int64_t)b * p.out_sb + (j0 + j) * q.out_st + (int64_t)h * p.out_sh + row, p.out_dtype, y);
+    }
+    __syncthreads();   // the next chunk restages
+  }
+}
+
+// ---- commit -----------------------------------------------------------------
+constexpr int kCommitTC = 16;   // tokens staged at a time
+
+template <int PB, int N, int TPR>
+__global__ void __launch_bounds__(128 * TPR) commit_step_kernel(const SpecParams q) {
+  constexpr int NC = N - PB;
+  const StepParams& p = q.sp;
+  constexpr int LPR = PB / 4;
+  constexpr int HCH = (LPR + TPR - 1) / TPR;
+  const int T = blockDim.x, tid = threadIdx.x;
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int Pn = p.P, c = p.c;
+  __shared__ float Bs[kCommitTC * PB], s_x[kCommitTC * 128];
+  __shared__ float s_dt[kCommitTC], s_dA[kCommitTC], s_dec[kCommitTC];
+  __shared__ int s_k, s_r;
+  const bool lead = (h == 0 && tid == 0);   // writes the row's flush_idx entry
+
+  const int slot = p.idx ? p.idx[b] : b;
+  if (slot == p.pad) {
+    if (lead) q.flush_idx[b] = -1;
+    return;
+  }
+  if (slot < 0 || slot >= p.S) {
+    if (lead) q.flush_idx[b] = -1;
+    if (tid == 0 && p.status) atomicOr(p.status, STATUS_BAD_SLOT);
+    return;
+  }
+  const int HG = p.H / p.G;
+  const int g = h / HG;
+  const int64_t sh = (int64_t)slot * p.H + h;
+  const int cp = ring_dt_stride(c);
+  int t0 = 0;
+  if (tid == 0) {
+    const int k = q.accept[b];
+    t0 = p.t[sh];
+    s_k = (k >= 0 && k <= q.ntok && t0 % c + k <= c) ? k : -1;
+    s_r = t0 % c;
+  }
+  __syncthreads();
+  const int k = s_k;
+  const int r = s_r;
+  if (k <= 0) {
+    if (lead) q.flush_idx[b] = -1;
+    if (k < 0 && tid == 0 && p.status) atomicOr(p.status, STATUS_SPEC_WINDOW);
+    return;
+  }
+  float4* hot4 = reinterpret_cast<float4*>(p.hot + sh * (int64_t)Pn * PB);
+  const int nh = Pn * LPR;
+  float4 hv[HCH];
+#pragma unroll
+  for (int kk = 0; kk < HCH; ++kk) {
+    const int i = kk * T + tid;
+    if (i < nh) hv[kk] = hot4[i];
+  }
+  const float A_h = p.A[h];
+  float glog = 0.0f;
+  if (tid == 0) glog = p.glog[sh];
+  for (int j0 = 0; j0 < k; j0 += kCommitTC) {
+    const int nt = min(kCommitTC, k - j0);
+    // ---- stage the nt tokens (x, B_hot, dt) and write their ring entries
+    for (int e = tid; e < nt * Pn; e += T) {
+      const int j = e / Pn, rr = e - j * Pn;
+      const float xv = ld_io(p.x, (int64_t)b * p.x_sb + (j0 + j) * q.x_st + (int64_t)h * p.x_sh + rr, p.io_dtype);
+      s_x[e] = xv;
+      st_io(p.ring_x, (sh * c + r + j0 + j) * Pn + rr, p.io_dtype, xv);
+    }
+    for (int e = tid; e < nt * PB; e += T) {
+      const int j = e / PB, n = e - j * PB;
+      Bs[e] = ld_io(p.B, (int64_t)b * p.B_sb + (j0 + j) * q.B_st + (int64_t)g * N + n, p.io_dtype);
+    }
+    if (h % HG == 0) {   // the group's B_cold, once per group
+      for (int e = tid; e < nt * NC; e += T) {
+        const int j = e / NC, n = e - j * NC;
+        p.ring_b[(((int64_t)slot * p.G + g) * c + r + j0 + j) * NC + n] =
+            ld_io(p.B, (int64_t)b * p.B_sb + (j0 + j) * q.B_st + (int64_t)g * N + PB + n, p.io_dtype);
+      }
+    }
+    if (tid < nt) {
+      const float d = spec_dt(p, b, h, (j0 + tid) * q.dt_st);
+      const float dA = d * A_h;
+      s_dt[tid] = d;
+      s_dA[tid] = dA;
+      s_dec[tid] = expf(dA);
+      p.ring_dt[sh * cp + r + j0 + tid] = d;
+    }
+    __syncthreads();
+    if (tid == 0)
+      for (int j = 0; j < nt; ++j) glog = glog + s_dA[j];   // in token order, as the steps
+    for (int j = 0; j < nt; ++j)
+      hot_token<PB, HCH>(hv, T, tid, nh, s_dt[j], s_dec[j], Bs + j * PB, nullptr, s_x + j * Pn, nullptr, false);
+    __syncthreads();   // the next chunk restages
+  }
+#pragma unroll
+  for (int kk = 0; kk < HCH; ++kk) {
+    const int i = kk * T + tid;
+    if (i < nh) hot4[i] = hv[kk];
+  }
+  if (tid == 0) {
+    const int t1 = t0 + k;
+    const bool flush = (t1 % c) == 0;
+    p.glog[sh] = flush ? 0.0f : glog;   // the FLUSH that follows re-bases the cold slice
+    p.t[sh] = t1;
+    if (h == 0) q.flush_idx[b] = flush ? slot : -1;
+  }
+}
+
+}  // namespace nssm

@@ -16,6 +16,10 @@ weights and cache must live on a CUDA device.
 Cold storage: ``cold="fp32"`` reproduces the reference's ``cold_bf16=0`` to fp32 rounding;
 ``"bf16"`` / ``"fp8"`` keep the cold slice only in that dtype (dequantise, replay,
 requantise every c tokens), where the reference re-snapshots a full fp32 state.
+``cold="off"`` is the hot-only self-speculative draft model (the reference's
+``install(..., cold="off")``, scale/v4_fused_decode.py:140-142 and :49-55): after the prefill
+split, every decode token runs ``draft_state_update`` on a draft copy of the hot slice, with no
+cold read, ring or flush.
 """
 from __future__ import annotations
 
@@ -24,7 +28,8 @@ import math
 import torch
 import torch.nn.functional as F
 
-from .ops import conv_step, gated_rmsnorm, mamba_chunk_scan_combined, prefill_split, rot_flat, tiered_state_update
+from .ops import (conv_step, draft_state_update, gated_rmsnorm, mamba_chunk_scan_combined, prefill_split, rot_flat,
+                  tiered_state_update)
 from .pool import TieredSlotPool
 
 _MODES = {(0, 0): "stale", (1, 0): "corr", (0, 1): "coldoff"}
@@ -95,6 +100,11 @@ def _decode(self, input_states, cache_params):
     A = -torch.exp(self.A_log.float())
     y = torch.empty(b, H, P, dtype=dtype, device=input_states.device)
     norm = self.norm
+    if st["cold"] == "off":   # hot-only draft: the first token after the prefill starts from the pool
+        draft_state_update(st["pool"], 0, st["draft"], x, dt[:, 0], A, Bv, Cv, self.D, self.dt_bias, True,
+                           st["slots"], -1, y, None, self.time_step_min, from_pool=st["draft_fresh"])
+        st["draft_fresh"] = False
+        return self.out_proj(_norm(self, y.reshape(b, 1, I), gate).to(dtype))
     if (all(hasattr(norm, a) for a in ("weight", "variance_epsilon", "group_size"))
             and norm.group_size == (H // G) * P):
         # the gated norm fused into the step (its group is one SSM group of a row)
@@ -190,11 +200,15 @@ def _dispatch(self, input_states, cache_params=None, attention_mask=None):
         b, H, P, N = ssm.shape
         pool = st["pool"]
         if pool is None or pool.S != b or pool.device != ssm.device:
-            pool = TieredSlotPool(1, b, H, P, N, self.n_groups, st["pb"], st["c"], st["cold"],
+            off = st["cold"] == "off"   # the draft never reads the cold slice, ring or chunk (the
+            storage, chunk = ("fp8", 4) if off else (st["cold"], st["c"])   # reference passes c = 1 << 20)
+            pool = TieredSlotPool(1, b, H, P, N, self.n_groups, st["pb"], chunk, storage,
                                   input_states.dtype, ssm.device, max_batch=b)
             st["pool"] = pool
             st["slots"] = torch.arange(b, dtype=torch.int32, device=ssm.device)
+            st["draft"] = pool.new_draft()[0] if st["cold"] == "off" else None
         prefill_split(pool, 0, ssm.contiguous(), st["slots"])
+        st["draft_fresh"] = True
     return out
 
 
@@ -205,7 +219,8 @@ def install(model, pb: int = 32, c: int = 16, cold: str | None = None, corr: int
     Argument names follow scale/v4_native_decode.py:247-256 (``cold_bf16=1`` means
     ``cold="bf16"``, ``0`` means ``"fp32"``); ``cold="fp8"`` is the fp8 storage;
     ``lean_prefill`` (default 1, as the reference's ``v4cfg.get("lean_prefill", 1)``) selects
-    the chunk-scan prefill."""
+    the chunk-scan prefill; ``cold="off"`` installs the hot-only draft model
+    (scale/v4_fused_decode.py:140-142)."""
     if cold is None:
         cold = "fp32" if cold_bf16 == 0 else "bf16"
     mode = _MODES.get((int(bool(corr)), int(bool(coldoff))))
@@ -215,7 +230,8 @@ def install(model, pb: int = 32, c: int = 16, cold: str | None = None, corr: int
     for m in model.modules():
         if type(m).__name__ == "NemotronHMamba2Mixer":
             orig = type(m).torch_forward
-            m._nssm = dict(pb=pb, c=c, cold=cold, mode=mode, pool=None, slots=None, orig=orig,
+            m._nssm = dict(pb=pb, c=c, cold=cold, mode=mode, pool=None, slots=None, orig=orig, draft=None,
+                           draft_fresh=True,
                            R=_rotation_and_act(m), lean_prefill=int(bool(lean_prefill)))
             m.torch_forward = _dispatch.__get__(m)
             n += 1

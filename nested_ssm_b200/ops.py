@@ -9,6 +9,10 @@
 * :func:`prefill_snapshot` / :func:`prefill_split` -- scale/vllm_v4_patch.py:123-137.
 * :func:`rot_flat` -- scale/vllm_v4_patch.py:41-45 (fp32 accumulation, cast back).
 * :func:`materialize` -- exact full fp32 state of slots (read-only).
+* :func:`draft_state_update` / :func:`verify_state_update` / :func:`commit_state_update` --
+  self-speculative decoding: the hot-only draft (install(cold="off"),
+  scale/v4_fused_decode.py:49-55 and :140-142) and the draft -> verify -> accept cycle that
+  scale/bench_selfspec_e2e.py times, on the tiered state.
 * :func:`mamba_chunk_scan_combined` -- the prefill chunked scan of the lean prefill
   (scale/v4_native_decode.py:209-216), mamba_ssm's argument order; its final states feed
   :func:`prefill_split`.
@@ -189,6 +193,127 @@ def tiered_state_update(pool: TieredSlotPool, layer: int, x, dt, A, B, C_, D=Non
     lib = _lib.load()
     _lib.check(lib.nssm_tiered_step(C.byref(pool.struct(layer)), C.byref(a), _stream(x.device)))
     return out
+
+
+def draft_state_update(pool: TieredSlotPool, layer: int, draft: torch.Tensor, x, dt, A, B, C_, D=None,
+                       dt_bias=None, dt_softplus=True, state_batch_indices=None, pad_slot_id=-1, out=None,
+                       R=None, dt_min=DEFAULT_DT_MIN, from_pool=False):
+    """One token of the hot-only draft model (the reference's install(cold="off"): the SSU on
+    the hot slice alone, scale/v4_fused_decode.py:49-55, :140-142); returns ``out`` [b, H, P].
+
+    ``draft`` is this layer's draft state, fp32 [S, H, P, hot_dim] indexed by slot
+    (``pool.new_draft()[layer]``).  ``from_pool=True`` (the cycle's first draft token) starts
+    from the pool's committed hot slice; otherwise the draft state is advanced in place.
+    ``y = C_hot . h + D x``; the pool itself is not written."""
+    if x.dtype != pool.io_dtype:
+        raise ValueError(f"x dtype {x.dtype} differs from the pool's io dtype {pool.io_dtype}")
+    if draft.dtype != torch.float32 or not draft.is_contiguous() or tuple(draft.shape) != tuple(pool.hot.shape[1:]):
+        raise ValueError(f"draft must be contiguous fp32 {tuple(pool.hot.shape[1:])}")
+    if R is not None and x.shape[0] > pool.max_batch:
+        raise ValueError(f"batch {x.shape[0]} exceeds the pool's max_batch {pool.max_batch}")
+    a, out, keep = build_step_args(x, dt, A, B, C_, D, dt_bias, dt_softplus, state_batch_indices,
+                                   pad_slot_id, out, R, dt_min, "stale", pool.workspace, pool.status,
+                                   nheads=pool.H)
+    _require_cuda(x, draft)
+    lib = _lib.load()
+    _lib.check(lib.nssm_draft_step(C.byref(pool.struct(layer)), draft.data_ptr(), 1 if from_pool else 0,
+                                   C.byref(a), _stream(x.device)))
+    return out
+
+
+def _token_inputs(pool, x, dt, B, C_, out, want_out=True):
+    """Token-0 views and token strides of multi-token inputs x [b, n, H, P], dt [b, n, H]
+    (or [b, n, H, P] expanded), B / C [b, n, G, N] or [b, n, G*N], out [b, n, H, P]."""
+    if x.dim() != 4 or x.stride(3) != 1:
+        raise ValueError(f"x must be [b, n, H, P] with unit inner stride, got {tuple(x.shape)}")
+    b, n = x.shape[:2]
+    if dt.dim() == 4:
+        dt = dt[..., 0]
+    if dt.dim() != 3 or tuple(dt.shape[:2]) != (b, n):
+        raise ValueError(f"dt must be [b, n, H], got {tuple(dt.shape)}")
+    bc = []
+    for name, v in (("B", B), ("C", C_)):
+        if v is None:
+            bc.append(None)
+            continue
+        if v.dim() == 4:
+            if v.stride(3) != 1 or v.stride(2) != v.shape[3]:
+                v = v.contiguous()
+            v = v.reshape(b, n, -1) if v.is_contiguous() else v.flatten(2)
+        if v.dim() != 3 or tuple(v.shape[:2]) != (b, n) or v.stride(2) != 1:
+            raise ValueError(f"{name} must be [b, n, G, N] or [b, n, G*N], got {tuple(v.shape)}")
+        bc.append(v)
+    if not want_out:
+        return dt, bc[0], bc[1], None
+    if out is None:
+        out = torch.empty(b, n, pool.H, pool.P, dtype=x.dtype, device=x.device)
+    if out.dim() != 4 or tuple(out.shape[:2]) != (b, n):
+        raise ValueError(f"out must be [b, n, H, P], got {tuple(out.shape)}")
+    return dt, bc[0], bc[1], out
+
+
+def _token_struct(n, x, dt, B, C_, out, accept=None):
+    t = _lib.NssmTokenArgs()
+    t.ntok = n
+    t.x_stride_t, t.dt_stride_t = x.stride(1), dt.stride(1)
+    t.B_stride_t = B.stride(1)
+    t.C_stride_t = C_.stride(1) if C_ is not None else 0
+    t.out_stride_t = out.stride(1) if out is not None else 0
+    t.accept = _ptr(accept)
+    return t
+
+
+def _spec_workspace(pool, b, n, with_rot):
+    lib = _lib.load()
+    nbytes = lib.nssm_spec_workspace_bytes(b, n, pool.G, pool.N, nssm_dtype(pool.io_dtype), 1 if with_rot else 0)
+    return torch.empty(max(nbytes, 256), dtype=torch.uint8, device=pool.device)
+
+
+def verify_state_update(pool: TieredSlotPool, layer: int, x, dt, A, B, C_, D=None, dt_bias=None,
+                        dt_softplus=True, state_batch_indices=None, pad_slot_id=-1, out=None, R=None,
+                        dt_min=DEFAULT_DT_MIN, mode="stale"):
+    """y of n drafted tokens per row from the committed tiered state, as n successive
+    :func:`tiered_state_update` calls would give them; returns ``out`` [b, n, H, P].  Read-only
+    on the pool.  x [b, n, H, P], dt [b, n, H], B / C [b, n, G, N]; every row needs
+    ``t % c + n <= c`` (checked on the device: bit 2 of the pool's status).  Modes "stale" and
+    "coldoff"."""
+    if x.dtype != pool.io_dtype:
+        raise ValueError(f"x dtype {x.dtype} differs from the pool's io dtype {pool.io_dtype}")
+    dt, B3, C3, out = _token_inputs(pool, x, dt, B, C_, out)
+    b, n = x.shape[:2]
+    ws = _spec_workspace(pool, b, n, R is not None)
+    a, _, keep = build_step_args(x[:, 0], dt[:, 0], A, B3[:, 0], C3[:, 0], D, dt_bias, dt_softplus,
+                                 state_batch_indices, pad_slot_id, out[:, 0], R, dt_min, mode, ws, pool.status,
+                                 nheads=pool.H)
+    t = _token_struct(n, x, dt, B3, C3, out)
+    lib = _lib.load()
+    _lib.check(lib.nssm_verify_step(C.byref(pool.struct(layer)), C.byref(a), C.byref(t), _stream(x.device)))
+    return out
+
+
+def commit_state_update(pool: TieredSlotPool, layer: int, accept, x, dt, A, B, dt_bias=None, dt_softplus=True,
+                        state_batch_indices=None, pad_slot_id=-1, R=None, dt_min=DEFAULT_DT_MIN) -> None:
+    """Make the first ``accept[b]`` of the n verified tokens of row b permanent: the pool ends
+    exactly as after ``accept[b]`` :func:`tiered_state_update` calls with those inputs (hot
+    slice, ring, glog, t, and the flush when they complete a chunk).  ``accept`` int32 [b] on
+    the device, each in 0..n; x, dt, B and R as given to :func:`verify_state_update`."""
+    if x.dtype != pool.io_dtype:
+        raise ValueError(f"x dtype {x.dtype} differs from the pool's io dtype {pool.io_dtype}")
+    dt, B3, _, _ = _token_inputs(pool, x, dt, B, None, None, want_out=False)
+    b, n = x.shape[:2]
+    acc = accept if (accept.dtype == torch.int32 and accept.is_contiguous()) else accept.to(torch.int32).contiguous()
+    if acc.numel() != b:
+        raise ValueError(f"accept has {acc.numel()} entries, x has {b} rows")
+    ws = _spec_workspace(pool, b, n, R is not None)
+    dummy = torch.empty(b, pool.H, pool.P, dtype=x.dtype, device=x.device)   # out is not written
+    a, _, keep = build_step_args(x[:, 0], dt[:, 0], A, B3[:, 0], B3[:, 0], None, dt_bias, dt_softplus,
+                                 state_batch_indices, pad_slot_id, dummy, R, dt_min, "stale", ws, pool.status,
+                                 nheads=pool.H)
+    _require_cuda(acc)
+    t = _token_struct(n, x, dt, B3, B3, None, acc)
+    t.C_stride_t = t.B_stride_t
+    lib = _lib.load()
+    _lib.check(lib.nssm_commit_step(C.byref(pool.struct(layer)), C.byref(a), C.byref(t), _stream(x.device)))
 
 
 def selective_state_update(state: torch.Tensor, x, dt, A, B, C_, D=None, z=None, dt_bias=None,

@@ -105,11 +105,25 @@ class TieredSlotPool:
         return tot
 
     def check_status(self) -> None:
-        """Raise if a kernel flagged a bad slot index since the last reset (synchronises)."""
+        """Raise if a kernel flagged an error since the last reset (synchronises): bit 0 a slot
+        index outside the pool, bit 1 a pipeline wait that timed out, bit 2 a verify / commit
+        window across a chunk boundary or an accept count out of range."""
         v = int(self.status.item())
         if v:
             self.status.zero_()
-            raise IndexError(f"nested_ssm: a kernel saw a slot index outside [0, {self.S}) (status {v})")
+            what = []
+            if v & 1:
+                what.append(f"a slot index outside [0, {self.S})")
+            if v & 2:
+                what.append("a pipeline wait timed out")
+            if v & 4:
+                what.append("a verify / commit window crosses a chunk boundary or accept is out of range")
+            raise IndexError(f"nested_ssm: {'; '.join(what) or 'error'} (status {v})")
+
+    def new_draft(self) -> torch.Tensor:
+        """A draft state for the hot-only self-speculative draft: fp32 [L, S, H, P, hot_dim]
+        (indexed by slot like the pool's hot slice; nssm_draft_step fills it)."""
+        return torch.zeros_like(self.hot)
 
     def reset_slots(self, slots: torch.Tensor) -> None:
         """Zero the bookkeeping of the given slots (state buffers untouched)."""

@@ -52,6 +52,7 @@ __all__ = [
     "dequantize_rows", "TieredPoolRef", "NativePoolRef", "prefill_split",
     "tiered_step", "native_step", "fresh_step", "materialize", "make_inputs",
     "make_params", "fp8_ordered_codes", "conv_step", "conv_split", "gated_rmsnorm",
+    "draft_step", "verify_steps", "commit_steps",
 ]
 
 FP8 = torch.float8_e4m3fn
@@ -449,6 +450,56 @@ def fresh_step(state: torch.Tensor, slots, x, dt_raw, B, C, A, D, dt_bias,
     state[s] = S
     out[rows] = torch.einsum("bhpn,bhn->bhp", S, Ch) + xf * D.float().view(1, H, 1)
     return out
+
+
+def draft_step(draft: torch.Tensor, slots, x, dt_raw, B, C, A, D, dt_bias,
+               clamp_min: float | None = 1e-3, pad_slot_id: int = -1) -> torch.Tensor:
+    """One token of the hot-only self-speculative draft on ``draft [S, H, P, pb]``: the
+    reference's install(cold="off"), i.e. selective_state_update on the hot slice alone
+    (scale/v4_fused_decode.py:49-55) with no cold read, ring or flush (:140-142).  Its y and
+    hot evolution are those of the tiered step in mode "coldoff" (scale/v4_native_decode.py:
+    118-127), which the golden fixtures pin."""
+    pb = draft.shape[-1]
+    return fresh_step(draft, slots, x, dt_raw, B[..., :pb], C[..., :pb], A, D, dt_bias, clamp_min, pad_slot_id)
+
+
+def _check_window(pool: TieredPoolRef, slots, n: int, pad_slot_id: int):
+    _, s = _valid_rows(slots, pad_slot_id)
+    r = pool.t[s] % pool.c
+    if bool((r + n > pool.c).any()):
+        raise ValueError("a verify / commit window crosses a chunk boundary")
+
+
+def verify_steps(pool: TieredPoolRef, slots, xs, dts, Bs, Cs, A, D, dt_bias, clamp_min: float | None = 1e-3,
+                 pad_slot_id: int = -1, mode: str = "stale") -> torch.Tensor:
+    """y [b, n, H, P] of n tokens (xs [b, n, H, P], dts [b, n, H], Bs / Cs [b, n, G, N]) read
+    against the committed state exactly as n successive ``tiered_step`` calls would read them;
+    the pool is left unchanged (the verify of the draft -> verify -> accept cycle that
+    scale/bench_selfspec_e2e.py times)."""
+    import copy
+    n = xs.shape[1]
+    _check_window(pool, slots, n, pad_slot_id)
+    work = copy.deepcopy(pool)
+    return torch.stack([tiered_step(work, slots, xs[:, j], dts[:, j], Bs[:, j], Cs[:, j], A, D, dt_bias,
+                                    clamp_min, pad_slot_id, mode) for j in range(n)], dim=1)
+
+
+def commit_steps(pool: TieredPoolRef, slots, accept, xs, dts, Bs, A, dt_bias, clamp_min: float | None = 1e-3,
+                 pad_slot_id: int = -1) -> None:
+    """Advance row i by its first ``accept[i]`` tokens: ``tiered_step`` on the rows that keep
+    token j, for j = 0 .. n-1 (the state update does not depend on the readout mode)."""
+    n = xs.shape[1]
+    accept = torch.as_tensor(accept).reshape(-1)
+    _check_window(pool, slots, 0, pad_slot_id)
+    _, s = _valid_rows(slots, pad_slot_id)
+    rows, _ = _valid_rows(slots, pad_slot_id)
+    if bool(((pool.t[s] % pool.c) + accept[rows] > pool.c).any()):
+        raise ValueError("a commit window crosses a chunk boundary")
+    for j in range(n):
+        sl = torch.as_tensor(slots).clone().reshape(-1)
+        sl[accept <= j] = pad_slot_id
+        tiered_step(pool, sl, xs[:, j], dts[:, j], Bs[:, j], Bs[:, j], A, torch.zeros_like(A), dt_bias, clamp_min,
+                    pad_slot_id)
 
 
 def materialize(pool: TieredPoolRef, slots, A) -> torch.Tensor:

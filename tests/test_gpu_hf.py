@@ -164,3 +164,35 @@ def test_hf_lean_prefill_multi_chunk_runs():
         full = materialize(st["pool"], 0, st["slots"], -torch.exp(m.A_log.float()))
         torch.cuda.synchronize()
         torch.testing.assert_close(full.cpu(), captured[m.layer_idx].cpu(), rtol=0, atol=0)
+
+
+def test_hf_hot_only_draft_install():
+    """install(cold="off"), the reference's hot-only draft model (scale/v4_fused_decode.py:
+    140-142): every decode token goes through the draft kernel, and its mixer outputs are those
+    of the tiered install in mode coldoff (the same hot evolution and hot-only readout,
+    scale/v4_native_decode.py:118-127) to fp32 rounding of the readout."""
+    from nested_ssm_b200.hf import install
+    d = GD.load("hf_generate.npz")
+    cfg = GD.MG.HF
+    torch.backends.cudnn.allow_tf32 = False
+    torch.backends.cuda.matmul.allow_tf32 = False
+    outs = []
+    for kw in (dict(cold="off"), dict(cold="fp32", coldoff=1)):
+        model = GD.MG.hf_model(cfg["seed"])
+        Rs = GD.MG.hf_rotations(model, cfg["seed"])
+        mixers = [m for m in model.modules() if type(m).__name__ == "NemotronHMamba2Mixer"]
+        for m, R in zip(mixers, Rs):
+            m.act = RotAct(m.act, m.intermediate_size, m.n_groups, m.ssm_state_size, R)
+        model = model.cuda()
+        install(model, pb=cfg["pb"], c=cfg["c"], **kw)
+        mo = _mixer_decode_outputs(mixers)
+        with torch.no_grad():
+            out = model.generate(d["ids"].cuda(), max_new_tokens=cfg["new"], do_sample=False)
+        outs.append((out.cpu(), mo, mixers))
+    (seq_d, mo_d, mix_d), (seq_c, mo_c, _) = outs
+    assert torch.equal(seq_d, seq_c)
+    for a, b in zip(mo_d, mo_c):
+        for ya, yb in zip(a, b):
+            torch.testing.assert_close(ya, yb, rtol=1e-3, atol=1e-4)
+    for m in mix_d:   # the draft kernel ran and the pool's bookkeeping never moved
+        assert m._nssm["draft"] is not None and int(m._nssm["pool"].t[0].max()) == 0

@@ -264,7 +264,7 @@ int launch_verify(const nssm::SpecParams& q, int batch, cudaStream_t st) {
     return fail(NSSM_ERR_UNSUPPORTED, "verify / commit need the persistent kernels' layout (16-byte aligned rows, "
                                       "headdim %% 4 == 0 and <= %d)", nssm::kPMaxPersistent);
   dim3 grid(q.sp.H, batch);
-  const int threads = round_up(q.sp.P * kTPR, 32);
+  const int threads = round_up(q.sp.P * 2, 32);   // two threads per headdim row
   const size_t smem = sizeof(float) * nssm::verify_smem_floats<PB, NC, COLD>(q.sp.P);
   auto fn = nssm::verify_step_kernel<PB, NC, COLD, kTPR>;
   if (smem > 48 * 1024) {

@@ -135,63 +135,46 @@ __global__ void __launch_bounds__(128 * TPR) draft_step_kernel(const SpecParams 
 }
 
 // ---- verify -----------------------------------------------------------------
-// Tokens are taken TC at a time: their x, B_hot, C and dt scalars are staged with one round of
-// loads (the item's cold rows are loaded in the same round), the cold partials of every staged
-// token are formed from the cold chunks decoded once, the hot recurrence runs through the
-// tokens in registers, and one pass writes their y -- two block barriers per TC tokens.
-// C_cold is staged in chunks of CE values at a padded stride CS, so the 128-bit shared reads
-// of any 8 consecutive threads (one quarter-warp) fall in distinct banks.
-template <int COLD> struct VerifyTC { static constexpr int kV = COLD == COLD_F32 ? 4 : 8; };
-
-template <int PB, int NC, int COLD>
-struct VerifyShape {
-  using Sh = StepShape<PB, NC, COLD>;
-  static constexpr int TC = VerifyTC<COLD>::kV;
-  static constexpr int CS = Sh::CE == 4 ? 4 : Sh::CE + 4;   // padded chunk stride (floats)
-  static constexpr int CW = Sh::CPR * CS;                    // C_cold floats per token
-  // dynamic shared floats: per staged token Bh, Ch [PB], Cc [CW], s_x, yh [P], pc [P * CPR];
-  // s_sco [P]; per staged token dt, dA, exp(dA), exp(glog) [4 * TC]
-  __host__ __device__ static constexpr size_t smem_floats(int P) {
-    return (size_t)TC * (2 * PB + CW + 2 * (size_t)P + (size_t)P * Sh::CPR) + (size_t)P + 4 * (size_t)TC;
-  }
-};
+// Two threads per headdim row: thread 2r + u holds half u of row r's hot slice (fp32, PB/2
+// values) and of its cold slice (decoded to fp32 once, the first ceil(CPR/2) 16-byte chunks for
+// u = 0, the rest for u = 1).  Tokens are staged TC at a time (x, B_hot, C and the dt scalars,
+// one round of loads); each thread then runs the hot recurrence of its half row through the
+// staged tokens and forms both partial dot products, and one shuffle combines the pair.  Every
+// lane of a warp reads the same B / C words (shared-memory broadcast).  Two block barriers per
+// TC tokens.  Headdim <= 80 (the persistent kernels' limit, which verify shares): <= 160 threads.
+constexpr int kVerifyTC = 16;
 
 template <int PB, int NC, int COLD>
 __host__ __device__ constexpr size_t verify_smem_floats(int P) {
-  return VerifyShape<PB, NC, COLD>::smem_floats(P);
+  // per staged token: B_hot, C_hot [PB], C_cold [NC], x [P]; dt, dA, exp(dA), exp(glog) [4 TC]
+  return (size_t)kVerifyTC * (2 * PB + NC + (size_t)P) + 4 * (size_t)kVerifyTC;
 }
 
 template <int PB, int NC, int COLD, int TPR>
-__global__ void __launch_bounds__(128 * TPR, COLD == COLD_FP8 ? 3 : 2) verify_step_kernel(const SpecParams q) {
+__global__ void __launch_bounds__(160, 4) verify_step_kernel(const SpecParams q) {
   const StepParams& p = q.sp;
   using Sh = StepShape<PB, NC, COLD>;
-  using VS = VerifyShape<PB, NC, COLD>;
   constexpr int N = Sh::N;
-  constexpr int LPR = Sh::LPR;
-  constexpr int CPR = Sh::CPR;
-  constexpr int CE = Sh::CE;
-  constexpr int CS = VS::CS;
-  constexpr int CW = VS::CW;
-  constexpr int HCH = (LPR + TPR - 1) / TPR;
-  constexpr int KCH = (CPR + TPR - 1) / TPR;
+  constexpr int CPR = Sh::CPR;        // 16-byte cold chunks per row
+  constexpr int CE = Sh::CE;          // values per chunk
+  constexpr int K0 = (CPR + 1) / 2;   // chunks of half 0 (half 1 takes CPR - K0)
+  constexpr int HQ = PB / 8;          // hot float4 per half row
   constexpr int kPerW = WordTraits<COLD>::kPer;
-  constexpr int TC = VS::TC;
+  constexpr int TC = kVerifyTC;
   static_assert(Sh::kCold, "tiered instances only");
-  static_assert(CE % 4 == 0, "cold chunks are whole float4s");
+  static_assert(PB % 8 == 0 && CE % 4 == 0, "half rows of whole float4s");
 
-  const int T = blockDim.x, tid = threadIdx.x;
+  const int tid = threadIdx.x;
   const int h = blockIdx.x, b = blockIdx.y;
   const int Pn = p.P, c = p.c;
-  const int ncc = Pn * CPR;
+  const int row = tid >> 1, u = tid & 1;
+  const bool act = row < Pn;
   extern __shared__ __align__(16) float smem[];
   float* Bh = smem;                 // [TC][PB]
   float* Ch = Bh + TC * PB;         // [TC][PB]
-  float* Cc = Ch + TC * PB;         // [TC][CW]   C_cold, chunk m at m * CS
-  float* s_x = Cc + TC * CW;        // [TC][P]
-  float* yh = s_x + TC * Pn;        // [TC][P]
-  float* pc = yh + TC * Pn;         // [TC][P * CPR]
-  float* s_sco = pc + TC * ncc;     // [P]
-  float* s_dt = s_sco + Pn;         // [TC]
+  float* Cc = Ch + TC * PB;         // [TC][NC]
+  float* s_x = Cc + TC * NC;        // [TC][P]
+  float* s_dt = s_x + TC * Pn;      // [TC]
   float* s_dA = s_dt + TC;          // [TC]
   float* s_dec = s_dA + TC;         // [TC]
   float* s_eg = s_dec + TC;         // [TC]
@@ -205,16 +188,32 @@ __global__ void __launch_bounds__(128 * TPR, COLD == COLD_FP8 ? 3 : 2) verify_st
   }
   const int g = h / (p.H / p.G);
   const int64_t sh = (int64_t)slot * p.H + h;
+  const bool cold_read = p.mode != NSSM_MODE_COLDOFF;
 
-  const int nh = Pn * LPR;
-  const float4* hot4 = reinterpret_cast<const float4*>(p.hot + sh * (int64_t)Pn * PB);
-  float4 hv[HCH];
+  // ---- this thread's half row: hot fp32, cold decoded once
+  float4 hv[HQ];
+  float cv[K0 * CE];
+  float scl = 0.0f;
+  const int kn = u == 0 ? K0 : CPR - K0;
+  if (act) {
+    const float4* hot4 = reinterpret_cast<const float4*>(p.hot + (sh * Pn + row) * PB) + u * HQ;
 #pragma unroll
-  for (int k = 0; k < HCH; ++k) {
-    const int i = k * T + tid;
-    if (i < nh) hv[k] = hot4[i];
+    for (int k = 0; k < HQ; ++k) hv[k] = hot4[k];
+    if (cold_read) {
+      const uint4* c16 = reinterpret_cast<const uint4*>(static_cast<const char*>(p.cold) +
+                                                        (sh * Pn + row) * (int64_t)(NC * Sh::ESZ)) + u * K0;
+#pragma unroll
+      for (int k = 0; k < K0; ++k) {
+        if (k < kn) {
+          const uint4 w = c16[k];
+          const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int wi = 0; wi < 4; ++wi) word_to_float<COLD>(wv[wi], cv + k * CE + wi * kPerW);
+        }
+      }
+      scl = (COLD == COLD_FP8) ? p.scale[sh * Pn + row] : 1.0f;
+    }
   }
-  if (tid < Pn) s_sco[tid] = (COLD == COLD_FP8) ? p.scale[sh * Pn + tid] : 1.0f;
   float glog = 0.0f;   // thread 0: glog before the next token to be read
   if (tid == 0) {
     const int r = p.t[sh] % c;
@@ -228,33 +227,25 @@ __global__ void __launch_bounds__(128 * TPR, COLD == COLD_FP8 ? 3 : 2) verify_st
   }
   const float A_h = p.A[h];
   const float Dh = p.D ? p.D[h] : 0.0f;
-  const bool cold_read = p.mode != NSSM_MODE_COLDOFF;
-  const uint4* cold16 = reinterpret_cast<const uint4*>(static_cast<const char*>(p.cold) + sh * (int64_t)Pn * NC * Sh::ESZ);
+  const int T = blockDim.x;
 
   for (int j0 = 0; j0 < q.ntok; j0 += TC) {
     const int nt = min(TC, q.ntok - j0);
-    // ---- one round of loads: the staged tokens' inputs and the item's cold rows
-    uint4 cw[KCH];
-    if (cold_read) {
-#pragma unroll
-      for (int k = 0; k < KCH; ++k) {
-        const int i = k * T + tid;
-        if (i < ncc) cw[k] = cold16[i];
-      }
-    }
-    for (int e = tid; e < nt * Pn; e += T) {
-      const int j = e / Pn, r = e - j * Pn;
-      s_x[e] = ld_io(p.x, (int64_t)b * p.x_sb + (j0 + j) * q.x_st + (int64_t)h * p.x_sh + r, p.io_dtype);
-    }
-    for (int e = tid; e < nt * N; e += T) {
-      const int j = e / N, n = e - j * N;
-      const int64_t row = (int64_t)(j0 + j);
-      if (n < PB) {
-        Bh[j * PB + n] = ld_io(p.B, (int64_t)b * p.B_sb + row * q.B_st + (int64_t)g * N + n, p.io_dtype);
-        Ch[j * PB + n] = ld_io(p.C, (int64_t)b * p.C_sb + row * q.C_st + (int64_t)g * N + n, p.io_dtype);
-      } else if (cold_read) {
-        const int m = (n - PB) / CE, u = (n - PB) - m * CE;
-        Cc[j * CW + m * CS + u] = ld_io(p.C, (int64_t)b * p.C_sb + row * q.C_st + (int64_t)g * N + n, p.io_dtype);
+    // ---- stage the nt tokens (one round of independent loads)
+    for (int j = 0; j < nt; ++j) {
+      const int64_t tok = j0 + j;
+      for (int r = tid; r < Pn; r += T)
+        s_x[j * Pn + r] = ld_io(p.x, (int64_t)b * p.x_sb + tok * q.x_st + (int64_t)h * p.x_sh + r, p.io_dtype);
+      const int64_t gb = (int64_t)b * p.B_sb + tok * q.B_st + (int64_t)g * N;
+      const int64_t gc = (int64_t)b * p.C_sb + tok * q.C_st + (int64_t)g * N;
+      for (int n = tid; n < N; n += T) {
+        const float cvv = ld_io(p.C, gc + n, p.io_dtype);
+        if (n < PB) {
+          Bh[j * PB + n] = ld_io(p.B, gb + n, p.io_dtype);
+          Ch[j * PB + n] = cvv;
+        } else {
+          Cc[j * NC + n - PB] = cvv;
+        }
       }
     }
     if (tid < nt) {
@@ -271,50 +262,49 @@ __global__ void __launch_bounds__(128 * TPR, COLD == COLD_FP8 ? 3 : 2) verify_st
         glog = glog + s_dA[j];
       }
     }
-    // ---- cold partials of every staged token from the chunks decoded once
-    if (cold_read) {
+    __syncthreads();
+    for (int j = 0; j < nt; ++j) {
+      float yhot = 0.0f, ycold = 0.0f;
+      float xp = 0.0f;
+      if (act) {
+        const float dt = s_dt[j], decay = s_dec[j];
+        xp = s_x[j * Pn + row];
+        const float4* b4 = reinterpret_cast<const float4*>(Bh + j * PB) + u * HQ;
+        const float4* c4 = reinterpret_cast<const float4*>(Ch + j * PB) + u * HQ;
 #pragma unroll
-      for (int k = 0; k < KCH; ++k) {
-        const int i = k * T + tid;
-        if (i < ncc) {
-          const uint32_t wv[4] = {cw[k].x, cw[k].y, cw[k].z, cw[k].w};
-          float qv[CE];
+        for (int k = 0; k < HQ; ++k) {
+          const float4 bb = b4[k], cc = c4[k];
+          float4 v = hv[k];
+          v.x = fmaf(v.x, decay, (dt * bb.x) * xp);
+          v.y = fmaf(v.y, decay, (dt * bb.y) * xp);
+          v.z = fmaf(v.z, decay, (dt * bb.z) * xp);
+          v.w = fmaf(v.w, decay, (dt * bb.w) * xp);
+          hv[k] = v;
+          yhot = fmaf(v.x, cc.x, fmaf(v.y, cc.y, fmaf(v.z, cc.z, fmaf(v.w, cc.w, yhot))));
+        }
+        if (cold_read) {
+          const float4* cc4 = reinterpret_cast<const float4*>(Cc + j * NC + u * K0 * CE);
 #pragma unroll
-          for (int wi = 0; wi < 4; ++wi) word_to_float<COLD>(wv[wi], qv + wi * kPerW);
-          const int coff = (i % CPR) * CS;
-          for (int j = 0; j < nt; ++j) {
-            const float4* c4 = reinterpret_cast<const float4*>(Cc + j * CW + coff);
-            float part = 0.0f;
+          for (int k = 0; k < K0; ++k) {
+            if (k < kn) {
 #pragma unroll
-            for (int v = 0; v < CE / 4; ++v) {
-              const float4 cv = c4[v];
-              part = fmaf(qv[4 * v], cv.x, part);
-              part = fmaf(qv[4 * v + 1], cv.y, part);
-              part = fmaf(qv[4 * v + 2], cv.z, part);
-              part = fmaf(qv[4 * v + 3], cv.w, part);
+              for (int v = 0; v < CE / 4; ++v) {
+                const float4 cc = cc4[k * (CE / 4) + v];
+                const float* qv = cv + k * CE + 4 * v;
+                ycold = fmaf(qv[0], cc.x, fmaf(qv[1], cc.y, fmaf(qv[2], cc.z, fmaf(qv[3], cc.w, ycold))));
+              }
             }
-            pc[j * ncc + i] = part;
           }
         }
       }
-    }
-    // ---- the hot recurrence through the staged tokens, row sums per token
-    for (int j = 0; j < nt; ++j)
-      hot_token<PB, HCH>(hv, T, tid, nh, s_dt[j], s_dec[j], Bh + j * PB, Ch + j * PB, s_x + j * Pn, yh + j * Pn,
-                         true);
-    __syncthreads();
-    // ---- y of every (token, row)
-    for (int e = tid; e < nt * Pn; e += T) {
-      const int j = e / Pn, row = e - j * Pn;
-      float y = yh[e];
-      if (cold_read) {
-        float yc = 0.0f;
-#pragma unroll
-        for (int cc = 0; cc < CPR; ++cc) yc += pc[j * ncc + row * CPR + cc];
-        y += (yc * s_sco[row]) * s_eg[j];
+      yhot += __shfl_xor_sync(0xffffffffu, yhot, 1);
+      ycold += __shfl_xor_sync(0xffffffffu, ycold, 1);
+      if (act && u == 0) {
+        float y = yhot;
+        if (cold_read) y += (ycold * scl) * s_eg[j];
+        if (p.D) y = fmaf(xp, Dh, y);
+        st_io(p.out, (int64_t)b * p.out_sb + (j0 + j) * q.out_st + (int64_t)h * p.out_sh + row, p.out_dtype, y);
       }
-      if (p.D) y = fmaf(s_x[e], Dh, y);
-      st_io(p.out, (int64_t)b * p.out_sb + (j0 + j) * q.out_st + (int64_t)h * p.out_sh + row, p.out_dtype, y);
     }
     __syncthreads();   // the next chunk restages
   }

@@ -263,10 +263,16 @@ int launch_verify(const nssm::SpecParams& q, int batch, cudaStream_t st) {
   if (!persistent_ok<PB, NC, COLD>(q.sp, &ring_ok))
     return fail(NSSM_ERR_UNSUPPORTED, "verify / commit need the persistent kernels' layout (16-byte aligned rows, "
                                       "headdim %% 4 == 0 and <= %d)", nssm::kPMaxPersistent);
+  // the tokens are staged in 16-byte chunks: token strides and headdim in whole chunks
+  const int iob = io_bytes(q.sp.io_dtype);
+  const int epc = 16 / iob;
+  if ((q.x_st * iob) % 16 || (q.B_st * iob) % 16 || (q.C_st * iob) % 16 || q.sp.P % epc)
+    return fail(NSSM_ERR_UNSUPPORTED, "verify needs token strides of whole 16-byte chunks and headdim %% %d == 0", epc);
   dim3 grid(q.sp.H, batch);
   const int threads = round_up(q.sp.P * 2, 32);   // two threads per headdim row
   const size_t smem = sizeof(float) * nssm::verify_smem_floats<PB, NC, COLD>(q.sp.P);
-  auto fn = nssm::verify_step_kernel<PB, NC, COLD, kTPR>;
+  auto fn = q.sp.io_dtype == NSSM_BF16 ? nssm::verify_step_kernel<PB, NC, COLD, true>
+                                       : nssm::verify_step_kernel<PB, NC, COLD, false>;
   if (smem > 48 * 1024) {
     int rc = ensure_smem_attr(reinterpret_cast<const void*>(fn));
     if (rc) return rc;

@@ -19,6 +19,7 @@
 #pragma once
 
 #include "nssm_device.cuh"
+#include "nssm_persistent.cuh"   // f2 and the packed fp32 helpers
 
 namespace nssm {
 
@@ -150,7 +151,24 @@ __host__ __device__ constexpr size_t verify_smem_floats(int P) {
   return (size_t)kVerifyTC * (2 * PB + NC + (size_t)P) + 4 * (size_t)kVerifyTC;
 }
 
-template <int PB, int NC, int COLD, int TPR>
+// 16 bytes of io values (8 bf16 or 4 fp32) as fp32 into shared memory
+template <bool IOBF>
+__device__ __forceinline__ void stage16(const void* src, float* dst) {
+  const uint4 v = *reinterpret_cast<const uint4*>(src);
+  if constexpr (IOBF) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+      reinterpret_cast<float4*>(dst)[i] = make_float4(__uint_as_float(w[2 * i] << 16), __uint_as_float(w[2 * i] & 0xffff0000u),
+                                                      __uint_as_float(w[2 * i + 1] << 16),
+                                                      __uint_as_float(w[2 * i + 1] & 0xffff0000u));
+  } else {
+    *reinterpret_cast<float4*>(dst) = make_float4(__uint_as_float(v.x), __uint_as_float(v.y), __uint_as_float(v.z),
+                                                  __uint_as_float(v.w));
+  }
+}
+
+template <int PB, int NC, int COLD, bool IOBF>
 __global__ void __launch_bounds__(160, 4) verify_step_kernel(const SpecParams q) {
   const StepParams& p = q.sp;
   using Sh = StepShape<PB, NC, COLD>;
@@ -190,8 +208,10 @@ __global__ void __launch_bounds__(160, 4) verify_step_kernel(const SpecParams q)
   const int64_t sh = (int64_t)slot * p.H + h;
   const bool cold_read = p.mode != NSSM_MODE_COLDOFF;
 
-  // ---- this thread's half row: hot fp32, cold decoded once
+  // ---- one round of loads: this thread's half row (hot fp32, raw cold chunks), the item's
+  //      bookkeeping and the first staged tokens; the cold chunks are decoded afterwards
   float4 hv[HQ];
+  uint4 craw[K0];
   float cv[K0 * CE];
   float scl = 0.0f;
   const int kn = u == 0 ? K0 : CPR - K0;
@@ -203,14 +223,8 @@ __global__ void __launch_bounds__(160, 4) verify_step_kernel(const SpecParams q)
       const uint4* c16 = reinterpret_cast<const uint4*>(static_cast<const char*>(p.cold) +
                                                         (sh * Pn + row) * (int64_t)(NC * Sh::ESZ)) + u * K0;
 #pragma unroll
-      for (int k = 0; k < K0; ++k) {
-        if (k < kn) {
-          const uint4 w = c16[k];
-          const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-          for (int wi = 0; wi < 4; ++wi) word_to_float<COLD>(wv[wi], cv + k * CE + wi * kPerW);
-        }
-      }
+      for (int k = 0; k < K0; ++k)
+        if (k < kn) craw[k] = c16[k];
       scl = (COLD == COLD_FP8) ? p.scale[sh * Pn + row] : 1.0f;
     }
   }
@@ -220,31 +234,33 @@ __global__ void __launch_bounds__(160, 4) verify_step_kernel(const SpecParams q)
     s_r = (r + q.ntok <= c) ? r : -1;
     glog = p.glog[sh];
   }
-  __syncthreads();
-  if (s_r < 0) {
-    if (tid == 0 && p.status) atomicOr(p.status, STATUS_SPEC_WINDOW);
-    return;
-  }
   const float A_h = p.A[h];
   const float Dh = p.D ? p.D[h] : 0.0f;
   const int T = blockDim.x;
 
   for (int j0 = 0; j0 < q.ntok; j0 += TC) {
     const int nt = min(TC, q.ntok - j0);
-    // ---- stage the nt tokens (one round of independent loads)
-    for (int j = 0; j < nt; ++j) {
-      const int64_t tok = j0 + j;
-      for (int r = tid; r < Pn; r += T)
-        s_x[j * Pn + r] = ld_io(p.x, (int64_t)b * p.x_sb + tok * q.x_st + (int64_t)h * p.x_sh + r, p.io_dtype);
-      const int64_t gb = (int64_t)b * p.B_sb + tok * q.B_st + (int64_t)g * N;
-      const int64_t gc = (int64_t)b * p.C_sb + tok * q.C_st + (int64_t)g * N;
-      for (int n = tid; n < N; n += T) {
-        const float cvv = ld_io(p.C, gc + n, p.io_dtype);
-        if (n < PB) {
-          Bh[j * PB + n] = ld_io(p.B, gb + n, p.io_dtype);
-          Ch[j * PB + n] = cvv;
+    // ---- stage the nt tokens: 16-byte chunks of x, B_hot and C, one per thread and pass
+    {
+      constexpr int EPC = IOBF ? 8 : 4;   // io values per 16-byte chunk
+      constexpr int IOB = IOBF ? 2 : 4;
+      const int xc = Pn / EPC, per = xc + PB / EPC + N / EPC;
+      const char* xb = static_cast<const char*>(p.x);
+      const char* bb = static_cast<const char*>(p.B);
+      const char* cb = static_cast<const char*>(p.C);
+      for (int e = tid; e < nt * per; e += T) {
+        const int j = e / per, k = e - j * per;
+        const int64_t tok = j0 + j;
+        if (k < xc) {
+          stage16<IOBF>(xb + ((int64_t)b * p.x_sb + tok * q.x_st + (int64_t)h * p.x_sh + k * EPC) * IOB,
+                        s_x + j * Pn + k * EPC);
+        } else if (k < xc + PB / EPC) {
+          const int n0 = (k - xc) * EPC;
+          stage16<IOBF>(bb + ((int64_t)b * p.B_sb + tok * q.B_st + (int64_t)g * N + n0) * IOB, Bh + j * PB + n0);
         } else {
-          Cc[j * NC + n - PB] = cvv;
+          const int n0 = (k - xc - PB / EPC) * EPC;
+          float* dst = n0 < PB ? Ch + j * PB + n0 : Cc + j * NC + (n0 - PB);
+          stage16<IOBF>(cb + ((int64_t)b * p.C_sb + tok * q.C_st + (int64_t)g * N + n0) * IOB, dst);
         }
       }
     }
@@ -255,7 +271,21 @@ __global__ void __launch_bounds__(160, 4) verify_step_kernel(const SpecParams q)
       s_dA[tid] = dA;
       s_dec[tid] = expf(dA);
     }
+    if (j0 == 0 && act && cold_read) {   // decode the cold chunks once
+#pragma unroll
+      for (int k = 0; k < K0; ++k) {
+        if (k < kn) {
+          const uint32_t wv[4] = {craw[k].x, craw[k].y, craw[k].z, craw[k].w};
+#pragma unroll
+          for (int wi = 0; wi < 4; ++wi) word_to_float<COLD>(wv[wi], cv + k * CE + wi * kPerW);
+        }
+      }
+    }
     __syncthreads();
+    if (s_r < 0) {   // uniform: the window crosses a chunk boundary
+      if (tid == 0 && p.status) atomicOr(p.status, STATUS_SPEC_WINDOW);
+      return;
+    }
     if (tid == 0) {   // the stale read of token j: glog + dA_0 + ... + dA_{j-1}, summed in token order
       for (int j = 0; j < nt; ++j) {
         s_eg[j] = expf(glog);
@@ -266,24 +296,27 @@ __global__ void __launch_bounds__(160, 4) verify_step_kernel(const SpecParams q)
     for (int j = 0; j < nt; ++j) {
       float yhot = 0.0f, ycold = 0.0f;
       float xp = 0.0f;
-      if (act) {
+      if (act) {   // packed fp32 pairs: the same per-element rounding as the scalar form
         const float dt = s_dt[j], decay = s_dec[j];
         xp = s_x[j * Pn + row];
+        const float2 dt2 = f2(dt, dt), x2 = f2(xp, xp), dec2 = f2(decay, decay);
         const float4* b4 = reinterpret_cast<const float4*>(Bh + j * PB) + u * HQ;
         const float4* c4 = reinterpret_cast<const float4*>(Ch + j * PB) + u * HQ;
+        float2 yh2 = f2(0.0f, 0.0f);
 #pragma unroll
         for (int k = 0; k < HQ; ++k) {
           const float4 bb = b4[k], cc = c4[k];
-          float4 v = hv[k];
-          v.x = fmaf(v.x, decay, (dt * bb.x) * xp);
-          v.y = fmaf(v.y, decay, (dt * bb.y) * xp);
-          v.z = fmaf(v.z, decay, (dt * bb.z) * xp);
-          v.w = fmaf(v.w, decay, (dt * bb.w) * xp);
-          hv[k] = v;
-          yhot = fmaf(v.x, cc.x, fmaf(v.y, cc.y, fmaf(v.z, cc.z, fmaf(v.w, cc.w, yhot))));
+          const float4 v = hv[k];
+          const float2 a = __ffma2_rn(f2(v.x, v.y), dec2, __fmul2_rn(__fmul2_rn(dt2, f2(bb.x, bb.y)), x2));
+          const float2 d = __ffma2_rn(f2(v.z, v.w), dec2, __fmul2_rn(__fmul2_rn(dt2, f2(bb.z, bb.w)), x2));
+          hv[k] = make_float4(a.x, a.y, d.x, d.y);
+          yh2 = __ffma2_rn(a, f2(cc.x, cc.y), yh2);
+          yh2 = __ffma2_rn(d, f2(cc.z, cc.w), yh2);
         }
+        yhot = yh2.x + yh2.y;
         if (cold_read) {
           const float4* cc4 = reinterpret_cast<const float4*>(Cc + j * NC + u * K0 * CE);
+          float2 yc2 = f2(0.0f, 0.0f);
 #pragma unroll
           for (int k = 0; k < K0; ++k) {
             if (k < kn) {
@@ -291,10 +324,12 @@ __global__ void __launch_bounds__(160, 4) verify_step_kernel(const SpecParams q)
               for (int v = 0; v < CE / 4; ++v) {
                 const float4 cc = cc4[k * (CE / 4) + v];
                 const float* qv = cv + k * CE + 4 * v;
-                ycold = fmaf(qv[0], cc.x, fmaf(qv[1], cc.y, fmaf(qv[2], cc.z, fmaf(qv[3], cc.w, ycold))));
+                yc2 = __ffma2_rn(f2(qv[0], qv[1]), f2(cc.x, cc.y), yc2);
+                yc2 = __ffma2_rn(f2(qv[2], qv[3]), f2(cc.z, cc.w), yc2);
               }
             }
           }
+          ycold = yc2.x + yc2.y;
         }
       }
       yhot += __shfl_xor_sync(0xffffffffu, yhot, 1);

@@ -287,9 +287,17 @@ int launch_commit(const nssm::SpecParams& q, int batch, cudaStream_t st) {
   if (!persistent_ok<PB, NC, COLD>(q.sp, &ring_ok))
     return fail(NSSM_ERR_UNSUPPORTED, "verify / commit need the persistent kernels' layout (16-byte aligned rows, "
                                       "headdim %% 4 == 0 and <= %d)", nssm::kPMaxPersistent);
+  // the tokens are staged in 16-byte chunks: token strides, headdim and the ring rows in whole chunks
+  const int iob = io_bytes(q.sp.io_dtype);
+  if ((q.x_st * iob) % 16 || (q.B_st * iob) % 16 || q.sp.P % (16 / iob) || !aligned16(q.sp.ring_x) ||
+      !aligned16(q.sp.ring_b))
+    return fail(NSSM_ERR_UNSUPPORTED, "commit needs token strides, headdim and ring rows of whole 16-byte chunks");
   dim3 grid(q.sp.H, batch);
   const int threads = round_up(q.sp.P * kTPR, 32);
-  nssm::commit_step_kernel<PB, PB + NC, kTPR><<<grid, threads, 0, st>>>(q);
+  if (q.sp.io_dtype == NSSM_BF16)
+    nssm::commit_step_kernel<PB, PB + NC, kTPR, true><<<grid, threads, 0, st>>>(q);
+  else
+    nssm::commit_step_kernel<PB, PB + NC, kTPR, false><<<grid, threads, 0, st>>>(q);
   int rc = cuda_check("commit_step_kernel launch");
   if (rc) return rc;
   nssm::StepParams fs = q.sp;   // FLUSH of the rows the commit completed (the others are -1)

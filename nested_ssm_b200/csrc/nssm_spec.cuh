@@ -348,7 +348,7 @@ __global__ void __launch_bounds__(160, 4) verify_step_kernel(const SpecParams q)
 // ---- commit -----------------------------------------------------------------
 constexpr int kCommitTC = 16;   // tokens staged at a time
 
-template <int PB, int N, int TPR>
+template <int PB, int N, int TPR, bool IOBF>
 __global__ void __launch_bounds__(128 * TPR) commit_step_kernel(const SpecParams q) {
   constexpr int NC = N - PB;
   const StepParams& p = q.sp;
@@ -357,7 +357,8 @@ __global__ void __launch_bounds__(128 * TPR) commit_step_kernel(const SpecParams
   const int T = blockDim.x, tid = threadIdx.x;
   const int h = blockIdx.x, b = blockIdx.y;
   const int Pn = p.P, c = p.c;
-  __shared__ float Bs[kCommitTC * PB], s_x[kCommitTC * 128];
+  __shared__ __align__(16) float Bs[kCommitTC * PB];
+  __shared__ __align__(16) float s_x[kCommitTC * 128];
   __shared__ float s_dt[kCommitTC], s_dA[kCommitTC], s_dec[kCommitTC];
   __shared__ int s_k, s_r;
   const bool lead = (h == 0 && tid == 0);   // writes the row's flush_idx entry
@@ -404,22 +405,34 @@ __global__ void __launch_bounds__(128 * TPR) commit_step_kernel(const SpecParams
   if (tid == 0) glog = p.glog[sh];
   for (int j0 = 0; j0 < k; j0 += kCommitTC) {
     const int nt = min(kCommitTC, k - j0);
-    // ---- stage the nt tokens (x, B_hot, dt) and write their ring entries
-    for (int e = tid; e < nt * Pn; e += T) {
-      const int j = e / Pn, rr = e - j * Pn;
-      const float xv = ld_io(p.x, (int64_t)b * p.x_sb + (j0 + j) * q.x_st + (int64_t)h * p.x_sh + rr, p.io_dtype);
-      s_x[e] = xv;
-      st_io(p.ring_x, (sh * c + r + j0 + j) * Pn + rr, p.io_dtype, xv);
-    }
-    for (int e = tid; e < nt * PB; e += T) {
-      const int j = e / PB, n = e - j * PB;
-      Bs[e] = ld_io(p.B, (int64_t)b * p.B_sb + (j0 + j) * q.B_st + (int64_t)g * N + n, p.io_dtype);
-    }
-    if (h % HG == 0) {   // the group's B_cold, once per group
-      for (int e = tid; e < nt * NC; e += T) {
-        const int j = e / NC, n = e - j * NC;
-        p.ring_b[(((int64_t)slot * p.G + g) * c + r + j0 + j) * NC + n] =
-            ld_io(p.B, (int64_t)b * p.B_sb + (j0 + j) * q.B_st + (int64_t)g * N + PB + n, p.io_dtype);
+    // ---- stage the nt tokens in 16-byte chunks (x -> shared and the ring, B_hot -> shared,
+    //      B_cold -> the ring by the group's first head) and their dt scalars
+    {
+      constexpr int EPC = IOBF ? 8 : 4;   // io values per 16-byte chunk
+      constexpr int IOB = IOBF ? 2 : 4;
+      const int xc = Pn / EPC;
+      const int bcn = (h % HG == 0) ? N / EPC : PB / EPC;   // B chunks this CTA needs
+      const int per = xc + bcn;
+      const char* xb = static_cast<const char*>(p.x);
+      const char* bb = static_cast<const char*>(p.B);
+      for (int e = tid; e < nt * per; e += T) {
+        const int j = e / per, kk = e - j * per;
+        const int64_t tok = j0 + j;
+        const int pos = r + j0 + j;
+        if (kk < xc) {
+          const uint4 v = *reinterpret_cast<const uint4*>(
+              xb + ((int64_t)b * p.x_sb + tok * q.x_st + (int64_t)h * p.x_sh + kk * EPC) * IOB);
+          *reinterpret_cast<uint4*>(static_cast<char*>(p.ring_x) + ((sh * c + pos) * Pn + kk * EPC) * IOB) = v;
+          stage16<IOBF>(&v, s_x + j * Pn + kk * EPC);
+        } else {
+          const int n0 = (kk - xc) * EPC;
+          const char* src = bb + ((int64_t)b * p.B_sb + tok * q.B_st + (int64_t)g * N + n0) * IOB;
+          if (n0 < PB) {
+            stage16<IOBF>(src, Bs + j * PB + n0);
+          } else {
+            stage16<IOBF>(src, p.ring_b + (((int64_t)slot * p.G + g) * c + pos) * NC + (n0 - PB));
+          }
+        }
       }
     }
     if (tid < nt) {

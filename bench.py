@@ -83,6 +83,20 @@ def parse():
     ap.add_argument("--model-prompt", type=int, default=8)
     ap.add_argument("--model-gen", type=int, default=32)
     ap.add_argument("--model-arms", default="ours,reference,hf")
+    ap.add_argument("--vllm-e2e", action="store_true",
+                    help="only the serving-engine decode (vLLM 0.22, stock against the tiered hook) and print its JSON")
+    ap.add_argument("--vllm-arms", default="vllm,ours")
+    ap.add_argument("--vllm-mem", type=float, default=0.6, help="vLLM gpu_memory_utilization, stock arm")
+    ap.add_argument("--vllm-mem-ours", type=float, default=0.6,
+                    help="vLLM gpu_memory_utilization with the hook (its tiered pools, max_num_seqs + 64 slots "
+                         "per layer, are allocated after vLLM's cache)")
+    ap.add_argument("--vllm-blocks", type=int, default=0, help="vLLM num_gpu_blocks_override (0: vLLM's choice)")
+    ap.add_argument("--vllm-arm", default=None, help=argparse.SUPPRESS)
+    ap.add_argument("--vllm-model", default=None, help=argparse.SUPPRESS)
+    ap.add_argument("--vllm-tokens", default=None, help=argparse.SUPPRESS)
+    ap.add_argument("--vllm-eager", action="store_true", help=argparse.SUPPRESS)
+    ap.add_argument("--vllm-reinit", action="store_true",
+                    help="replace vLLM's dummy weights by seeded BASELINE-distribution weights (token checks)")
     return ap.parse_args()
 
 
@@ -1005,6 +1019,9 @@ def multi_gpu_check(args, rank: int, ws: int):
                      "bit-identical to one GPU serving the whole global batch"}
 
 
+NEMOTRON_9B_LAYOUT = "M-M-M-MM-M-M-M*-M-M-M*-M-M-M-M*-M-M-M-M*-M-MM-M-M-M-M-M-"   # the published 9B-v2 layout
+
+
 def nemotron_h_9b(device="cuda", chunk_size=8):
     """The BASELINE's end-to-end architecture (Nemotron-H 9B), random init, bf16: hidden 4480,
     56 layers = 27 Mamba2 (128 heads x 80, d_state 128, 8 groups, conv 4) + 4 GQA attention
@@ -1018,7 +1035,7 @@ def nemotron_h_9b(device="cuda", chunk_size=8):
     8-token prompt and chunk 8, but 481 GB for the first at the published chunk 128."""
     from transformers import NemotronHConfig, NemotronHForCausalLM
     from transformers.models.nemotron_h import modeling_nemotron_h as MH
-    layout = "M-M-M-MM-M-M-M*-M-M-M*-M-M-M-M*-M-M-M-M*-M-MM-M-M-M-M-M-"   # the published 9B-v2 layout
+    layout = NEMOTRON_9B_LAYOUT
     kinds = {"M": "mamba", "*": "attention", "-": "moe"}
     cfg = NemotronHConfig(hidden_size=4480, layers_block_type=[kinds[ch] for ch in layout],
                           num_hidden_layers=len(layout), mamba_num_heads=128, mamba_head_dim=80,
@@ -1105,6 +1122,245 @@ def model_e2e(args, device="cuda", build=None):
             torch.cuda.empty_cache()
             torch.cuda.reset_peak_memory_stats()
     return out
+
+
+# --------------------------------------------------------------------------
+# serving-engine decode: vLLM 0.22, stock against the tiered hook (reduced BASELINE config 4)
+# --------------------------------------------------------------------------
+def vllm_model_dir(root: str) -> str:
+    """A model directory holding only the Nemotron-H 9B config (vLLM's own NemotronH config
+    class reads the "-" MLP layers); the weights are vLLM's dummy initialisation."""
+    d = os.path.join(root, "nemotron_h_9b")
+    os.makedirs(d, exist_ok=True)
+    cfg = {"architectures": ["NemotronHForCausalLM"], "model_type": "nemotron_h", "vocab_size": 131072,
+           "hidden_size": 4480, "intermediate_size": 15680, "num_hidden_layers": len(NEMOTRON_9B_LAYOUT),
+           "hybrid_override_pattern": NEMOTRON_9B_LAYOUT, "num_attention_heads": 40, "head_dim": 128,
+           "num_key_value_heads": 8, "mlp_hidden_act": "relu2", "ssm_state_size": 128, "mamba_num_heads": 128,
+           "mamba_n_groups": 8, "mamba_head_dim": 80, "mamba_d_conv": 4, "mamba_expand": 2,
+           "mamba_chunk_size": 128, "max_position_embeddings": 8192, "torch_dtype": "bfloat16",
+           "initializer_range": 0.02, "layer_norm_epsilon": 1e-5, "tie_word_embeddings": False,
+           "bos_token_id": 1, "eos_token_id": 2, "pad_token_id": 0}
+    with open(os.path.join(d, "config.json"), "w") as f:
+        json.dump(cfg, f)
+    return d
+
+
+# vLLM's dummy weights never pass through load_weights (where the hook applies its checkpoint),
+# so the shadow copy applies it at the end of NemotronHForCausalLM.__init__ as well
+_VLLM_INIT_ANCHOR = ("        self.make_empty_intermediate_tensors = (\n"
+                     "            self.model.make_empty_intermediate_tensors\n"
+                     "        )\n")
+_VLLM_INIT_TEXT = ("        from nested_ssm_b200 import vllm_hook as _nssm\n"
+                   "        _nssm.apply_ckpt(self)  # [nested_ssm] dummy weights: load_weights is not called\n")
+
+
+def vllm_shadow(root: str) -> str:
+    """A shadow of the installed vllm package under ``root`` (directories, file symlinks) whose
+    mamba_mixer2.py and nemotron_h.py are patched copies (the hook's five anchors and the init
+    call); returns the directory to put first on PYTHONPATH.  The installed package is not
+    modified."""
+    import importlib.util
+    import shutil
+    from nested_ssm_b200 import vllm_hook as VH
+    src = os.path.dirname(importlib.util.find_spec("vllm").origin)
+    top = os.path.join(root, "shadow")
+    dst = os.path.join(top, "vllm")
+    if not os.path.isdir(dst):
+        os.makedirs(top, exist_ok=True)
+        subprocess.run(["cp", "-rs", src, dst], check=True)
+        for rel in (VH.MIXER, VH.NEMOTRON):
+            path = os.path.join(dst, rel)
+            os.remove(path)
+            shutil.copyfile(os.path.join(src, rel), path)
+        VH.install(dst)
+        path = os.path.join(dst, VH.NEMOTRON)
+        with open(path) as f:
+            text, _ = VH.patch_source(f.read(), "after", _VLLM_INIT_ANCHOR, _VLLM_INIT_TEXT, VH.NEMOTRON)
+        with open(path, "w") as f:
+            f.write(text)
+    return top
+
+
+def vllm_rotation_ckpt(root: str, identity: bool = False, mixers: int = 27, G_: int = 8, N_: int = 128) -> str:
+    """Seeded orthogonal rotations (or identities) in the hook's checkpoint format {i: R_i [G, N, N]}."""
+    path = os.path.join(root, "rot_identity.pt" if identity else "rot.pt")
+    g = torch.Generator().manual_seed(7)
+    torch.save({i: (torch.eye(N_).repeat(G_, 1, 1) if identity
+                    else torch.linalg.qr(torch.randn(G_, N_, N_, generator=g))[0].contiguous()) for i in range(mixers)},
+               path)
+    return path
+
+
+def vllm_e2e(args):
+    """Reduced BASELINE config 4 in a serving engine: vLLM 0.22 (CUDA-graph decode, its own
+    fused Mamba2 kernels) on a dummy-weight Nemotron-H 9B, B sequences of `--model-prompt`
+    random tokens, `--model-gen` greedy tokens; decode = generate(gen + 1) - generate(1).
+    Arms: `vllm` (stock: fresh fp32 full state, vLLM's selective_state_update), `ours` (the same
+    engine with the tiered decode installed by nested_ssm_b200.vllm_hook: rotations from a
+    seeded checkpoint, fp8 cold, c = 4, the stale readout) and `ours_exact` (identity rotations,
+    fp32 cold, the exact rank-c correction readout: the tiered op's exact configuration, whose
+    greedy tokens are compared with the stock arm's as a check that the hook runs correctly
+    inside the engine; with `--vllm-reinit` the weights make the tokens depend on the state).  Each arm runs in its own
+    process; both use an fp32 SSM cache (mamba_ssm_cache_dtype), the reference's setting."""
+    root = tempfile.mkdtemp(prefix="nssm_vllm_")
+    model = vllm_model_dir(root)
+    out = {"config": {"workload": f"reduced BASELINE config 4 in vLLM 0.22: dummy-weight Nemotron-H 9B, bf16, "
+                                  f"B={args.model_batch}, prompt {args.model_prompt}, {args.model_gen} greedy tokens, "
+                                  "one GPU, decode = generate(K+1) - generate(1)",
+                      "batch": args.model_batch, "prompt": args.model_prompt, "gen": args.model_gen,
+                      "gpu_memory_utilization": {"vllm": args.vllm_mem, "ours": args.vllm_mem_ours}}, "arms": {}}
+    for arm in [a for a in args.vllm_arms.split(",") if a]:
+        env = dict(os.environ)
+        env["PYTHONPATH"] = REPO + (os.pathsep + env["PYTHONPATH"] if env.get("PYTHONPATH") else "")
+        base = arm[:-len("_eager")] if arm.endswith("_eager") else arm   # _eager: no CUDA graphs
+        if base in ("ours", "ours_exact"):
+            exact = base == "ours_exact"
+            env["PYTHONPATH"] = vllm_shadow(root) + os.pathsep + env["PYTHONPATH"]
+            env.update(NESTED_SSM_CKPT=vllm_rotation_ckpt(root, identity=exact), NESTED_SSM_MODE="v4",
+                       NESTED_SSM_PB="32", NESTED_SSM_C="4", NESTED_SSM_COLD="fp32" if exact else "fp8",
+                       NESTED_SSM_READOUT="corr" if exact else "stale")
+        cmd = [sys.executable, os.path.join(REPO, "bench.py"), "--vllm-arm", arm, "--vllm-model", model,
+               "--vllm-tokens", os.path.join(root, f"tokens_{arm}.pt"),
+               "--model-batch", str(args.model_batch), "--model-prompt", str(args.model_prompt),
+               "--model-gen", str(args.model_gen),
+               "--vllm-mem", str(args.vllm_mem if arm.startswith("vllm") else args.vllm_mem_ours),
+               "--vllm-blocks", str(args.vllm_blocks)] + (["--vllm-reinit"] if args.vllm_reinit else []) + \
+              (["--vllm-eager"] if arm.endswith("_eager") else [])
+        r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=1800)
+        line = next((ln for ln in reversed(r.stdout.splitlines()) if ln.startswith("{")), None)
+        text = (r.stderr or "") + (r.stdout or "")
+        if r.returncode != 0 or line is None:
+            errs = [ln.strip()[-300:] for ln in text.splitlines() if "Error" in ln or "error" in ln][:6]
+            out["arms"][arm] = {"unavailable": f"exit {r.returncode}", "errors": errs, "tail": text[-400:]}
+            continue
+        res = json.loads(line)
+        keys = ("[nested_ssm]", "KV cache size", "Maximum concurrency", "Graph capturing finished", "cudagraph_mode")
+        res["log"] = [ln.strip()[-200:] for ln in text.splitlines() if any(k in ln for k in keys)][:8]
+        import re
+        m = re.search(r"Maximum concurrency for (\d+) tokens per request: ([\d.]+)x", text)
+        if m:   # the per-token rate assumes all B rows decode together
+            res["max_concurrency"] = float(m.group(2))
+            res["all_rows_concurrent"] = float(m.group(2)) >= args.model_batch
+        out["arms"][arm] = res
+    ref = os.path.join(root, "tokens_vllm.pt")
+    for arm in [a for a in out["arms"] if a != "vllm"]:   # e.g. vllm_eager: stock against stock
+        mine = os.path.join(root, f"tokens_{arm}.pt")
+        if arm in out["arms"] and os.path.exists(ref) and os.path.exists(mine):
+            ra, rb = torch.load(ref), torch.load(mine)
+            a, b = ra["tokens"], rb["tokens"]
+            o = out["arms"][arm]
+            o["greedy_tokens_equal_to_stock"] = round(float((a == b).float().mean()), 4)
+            o["first_token_equal_to_stock"] = round(float((a[:, 0] == b[:, 0]).float().mean()), 4)
+            # while both arms have produced the same tokens, they score the same contexts: the
+            # sampled token's log-probability then measures how far the decode outputs differ
+            same = torch.cumprod((a == b).to(torch.int32), dim=1).bool()
+            if ra["logprobs"] is not None and rb["logprobs"] is not None and bool(same[:, 1:].any()):
+                d = (ra["logprobs"] - rb["logprobs"]).abs()[:, 1:][same[:, 1:]]
+                o["decode_logprob_abs_diff_on_common_prefix"] = {"max": round(float(d.max()), 5),
+                                                                 "mean": round(float(d.mean()), 6),
+                                                                 "tokens": int(d.numel())}
+            div = torch.where((~same).any(1), (~same).float().argmax(1), torch.full_like(a[:, 0], a.shape[1]))
+            o["first_divergence_mean_position"] = round(float(div.float().mean()), 2)
+    return out
+
+
+def _vllm_reinit(model):
+    """Seeded weights with the BASELINE's distributions in place of vLLM's dummy ones (which are
+    so small that every layer's output vanishes next to the embedding, so the greedy tokens would
+    not depend on the Mamba state): N(0, 0.02) matrices, A = -exp(U(0, ln 16)), dt_bias =
+    softplus^-1(U(1e-3, 0.1)), D and norm weights 1, biases 0.  Each parameter's draw is seeded by
+    its name, so every arm gets the same model.  The hook's cached fp32 copies of A, D and dt_bias
+    are refreshed in place."""
+    import math as m_
+    import zlib
+    with torch.inference_mode():   # the hook's caches were made inside vLLM's inference mode
+        for name, p in sorted(model.named_parameters()):
+            g = torch.Generator(device=p.device)
+            g.manual_seed(zlib.crc32(name.encode()))
+            if name.endswith(".A"):
+                p.copy_(-torch.exp(torch.rand(p.shape, generator=g, device=p.device) * m_.log(16.0)))
+            elif name.endswith("dt_bias"):
+                u = torch.rand(p.shape, generator=g, device=p.device) * (0.1 - 1e-3) + 1e-3
+                p.copy_(torch.log(torch.expm1(u)))
+            elif name.endswith(".D") or "norm" in name:
+                p.fill_(1.0)
+            elif name.endswith("bias"):
+                p.zero_()
+            else:
+                p.copy_(torch.randn(p.shape, generator=g, device=p.device, dtype=torch.float32) * 0.02)
+        for mod in model.modules():
+            st = getattr(mod, "nssm", None)
+            if isinstance(st, dict) and "A" in st:
+                st["A"].copy_(mod.A.detach().float().reshape(-1))
+                st["D"].copy_(mod.D.detach().float().reshape(-1))
+                st["dt_bias"].copy_(mod.dt_bias.detach().float().reshape(-1))
+    return True
+
+
+def _vllm_pool_stats(model):
+    """The tiered pools' bookkeeping after a run (hooked arms): how many mixers hold a pool, the
+    largest token count t, and the pools' status words."""
+    n, tmax, status = 0, 0, 0
+    for mod in model.modules():
+        st = getattr(mod, "nssm", None)
+        if isinstance(st, dict) and st.get("pool") is not None:
+            n += 1
+            tmax = max(tmax, int(st["pool"].t.max()))
+            status |= int(st["pool"].status.item())
+    return {"mixers_with_pool": n, "t_max": tmax, "status": status}
+
+
+def vllm_arm(args):
+    """One arm of vllm_e2e, in its own process (the parent chose the vllm package by PYTHONPATH)."""
+    import vllm
+    from vllm import LLM, SamplingParams
+    from vllm.inputs import TokensPrompt
+    from vllm.transformers_utils.config import _CONFIG_REGISTRY
+    # transformers' own NemotronH config has no dense-MLP ("-") layers; vLLM ships one that does
+    _CONFIG_REGISTRY["nemotron_h"] = "NemotronHConfig"
+    B, T, K = args.model_batch, args.model_prompt, args.model_gen
+    if args.vllm_reinit:   # apply_model sends the function to the engine's worker process
+        os.environ["VLLM_ALLOW_INSECURE_SERIALIZATION"] = "1"
+    kw = dict(model=args.vllm_model, skip_tokenizer_init=True, load_format="dummy", dtype="bfloat16",
+              max_num_seqs=B, max_model_len=T + K + 16, gpu_memory_utilization=args.vllm_mem,
+              enable_prefix_caching=False, seed=0, mamba_ssm_cache_dtype="float32")
+    if args.vllm_blocks:
+        kw["num_gpu_blocks_override"] = args.vllm_blocks
+    if args.vllm_eager:
+        kw["enforce_eager"] = True
+    llm = LLM(**kw)
+    if args.vllm_reinit:
+        llm.apply_model(_vllm_reinit)
+    g = torch.Generator().manual_seed(1)
+    prompts = [TokensPrompt(prompt_token_ids=r) for r in torch.randint(1000, 30000, (B, T), generator=g).tolist()]
+
+    def run(n):
+        sp = SamplingParams(max_tokens=n, ignore_eos=True, temperature=0.0, detokenize=False, logprobs=0)
+        t0 = time.perf_counter()
+        outs = llm.generate(prompts, sp, use_tqdm=False)
+        return time.perf_counter() - t0, outs
+
+    run(4)   # warm-up
+    t1, _ = run(1)
+    tk, outs = run(K + 1)
+    dec = (tk - t1) / K
+    toks = torch.tensor([list(o.outputs[0].token_ids) for o in outs])   # LLM.generate keeps prompt order
+    lps = torch.tensor([[float(d[t].logprob) for d, t in zip(o.outputs[0].logprobs, o.outputs[0].token_ids)]
+                        for o in outs]) if outs[0].outputs[0].logprobs else None
+    if args.vllm_tokens:
+        torch.save({"tokens": toks, "logprobs": lps}, args.vllm_tokens)
+    pools = None
+    if os.environ.get("NESTED_SSM_MODE") == "v4" and os.environ.get("VLLM_ALLOW_INSECURE_SERIALIZATION") == "1":
+        pools = llm.apply_model(_vllm_pool_stats)
+    res = {"decode_ms_per_token": round(dec * 1e3, 2), "decode_tokens_per_s": round(B / dec, 1),
+           "prefill_plus_one_s": round(t1, 3), "tokens": int(toks.numel()), "vllm": vllm.__version__,
+           "vllm_path": os.path.dirname(vllm.__file__),
+           "tiered_hook": os.environ.get("NESTED_SSM_MODE") == "v4",
+           "cold": os.environ.get("NESTED_SSM_COLD") if os.environ.get("NESTED_SSM_MODE") == "v4" else None,
+           "readout": os.environ.get("NESTED_SSM_READOUT") if os.environ.get("NESTED_SSM_MODE") == "v4" else None,
+           "pools": pools}
+    print(json.dumps(res), flush=True)
+    return 0
 
 
 # --------------------------------------------------------------------------
@@ -1213,6 +1469,11 @@ def main():
         return 0
     if args.reference_gpu_leg_only:
         print(json.dumps(reference_gpu_leg()), flush=True)
+        return 0
+    if args.vllm_arm:
+        return vllm_arm(args)
+    if args.vllm_e2e:
+        print(json.dumps({"vllm_e2e": vllm_e2e(args)}), flush=True)
         return 0
     if args.model_e2e:
         if not torch.cuda.is_available():

@@ -9,6 +9,11 @@ stays stock and the mode is chosen by the environment (``scale/vllm_v4_patch.py:
                                             v4: the tiered decode state op (default fresh)
     NESTED_SSM_PB=32  NESTED_SSM_C=4        hot width and flush period
     NESTED_SSM_COLD=fp32|bf16|fp8           cold storage (default bf16)
+    NESTED_SSM_READOUT=stale|corr|coldoff   v4 readout (default stale, the reference's; corr is
+                                            the exact rank-c correction of
+                                            scale/v4_native_decode.py:81-117, coldoff the
+                                            hot-only readout; an extension of the reference's
+                                            configuration)
 
 Checkpoint (``scale/vllm_v4_patch.py:59-84``): ``torch.save``'d dict ``{i: R_i [G, N, N]}`` with
 one rotation per Mamba2 mixer in model order, plus optionally ``"decay": {"A_log": [...],
@@ -47,6 +52,7 @@ MARK = "[nested_ssm]"
 NULL_BLOCK_ID = 0   # vllm/v1/attention/backends/utils.py:45 (padded decode entries)
 _MODES = ("fresh", "v4")
 _COLDS = ("fp32", "bf16", "fp8")
+_READOUTS = ("stale", "corr", "coldoff")
 
 
 # --------------------------------------------------------------------------
@@ -60,11 +66,14 @@ def config_from_env(env=None) -> dict | None:
     if not ck:
         return None
     cfg = dict(ckpt=ck, mode=env.get("NESTED_SSM_MODE", "fresh"), pb=int(env.get("NESTED_SSM_PB", "32")),
-               c=int(env.get("NESTED_SSM_C", "4")), cold=env.get("NESTED_SSM_COLD", "bf16"))
+               c=int(env.get("NESTED_SSM_C", "4")), cold=env.get("NESTED_SSM_COLD", "bf16"),
+               readout=env.get("NESTED_SSM_READOUT", "stale"))
     if cfg["mode"] not in _MODES:
         raise ValueError(f"NESTED_SSM_MODE={cfg['mode']!r}: expected one of {_MODES}")
     if cfg["cold"] not in _COLDS:
         raise ValueError(f"NESTED_SSM_COLD={cfg['cold']!r}: expected one of {_COLDS}")
+    if cfg["readout"] not in _READOUTS:
+        raise ValueError(f"NESTED_SSM_READOUT={cfg['readout']!r}: expected one of {_READOUTS}")
     if cfg["c"] < 1 or cfg["pb"] < 1:
         raise ValueError("NESTED_SSM_C and NESTED_SSM_PB must be positive")
     return cfg
@@ -133,9 +142,9 @@ def apply_ckpt(model, env=None) -> int:
         if cfg["mode"] == "v4":
             if getattr(m, "num_spec", 0):
                 raise NotImplementedError("nested_ssm vLLM hook: speculative decoding is not supported")
-            m.nssm = dict(pb=cfg["pb"], c=cfg["c"], cold=cfg["cold"], pool=None)
+            m.nssm = dict(pb=cfg["pb"], c=cfg["c"], cold=cfg["cold"], readout=cfg["readout"], pool=None)
     print(f"{MARK} ckpt {cfg['ckpt']} applied to {len(mixers)} mixers (mode={cfg['mode']} "
-          f"pb={cfg['pb']} c={cfg['c']} cold={cfg['cold']})", flush=True)
+          f"pb={cfg['pb']} c={cfg['c']} cold={cfg['cold']} readout={cfg['readout']})", flush=True)
     return len(mixers)
 
 
@@ -152,26 +161,82 @@ def rotate(mixer, B: torch.Tensor, C: torch.Tensor):
     return rot_flat(B, R), rot_flat(C, R)
 
 
+class SlotMap:
+    """vLLM block id -> tiered-pool slot.  vLLM 0.22 indexes a Mamba layer's state by block id
+    over the whole block pool it shares with the other layer groups (a layer's state tensor has
+    num_blocks rows, of which one per live request is used), so the tiered pool is sized by the
+    number of concurrent sequences and reached through this map.  A block keeps its slot while
+    it is mapped; when a prefill needs slots and none is free, the slots of blocks that are in
+    neither this step's decode batch nor its prefill rows (finished requests) are reclaimed."""
+
+    def __init__(self, num_slots: int):
+        self.num_slots = num_slots
+        self.of_block: dict[int, int] = {}
+        self.free = list(range(num_slots - 1, -1, -1))
+
+    def assign(self, blocks: list[int], live: list[int]) -> tuple[list[int], list[int]]:
+        """Slots for the prefill rows' ``blocks``; returns (slots, blocks unmapped by a
+        reclamation).  ``live``: this step's decode blocks."""
+        need = [k for k in dict.fromkeys(blocks) if k not in self.of_block]
+        freed = []
+        if len(need) > len(self.free):
+            keep = set(blocks) | set(live)
+            for k in [k for k in self.of_block if k not in keep]:
+                self.free.append(self.of_block.pop(k))
+                freed.append(k)
+            if len(need) > len(self.free):
+                raise RuntimeError(f"nested_ssm vLLM hook: {len(self.of_block) + len(need)} live sequences exceed "
+                                   f"the tiered pool's {self.num_slots} slots (NESTED_SSM_SLOTS)")
+        for k in need:
+            self.of_block[k] = self.free.pop()
+        return [self.of_block[k] for k in blocks], freed
+
+
+def _max_num_seqs() -> int:
+    try:
+        from vllm.config import get_current_vllm_config
+        return int(get_current_vllm_config().scheduler_config.max_num_seqs)
+    except Exception:   # outside a vLLM engine (tests)
+        return 256
+
+
 def _pool(mixer, ssm_state: torch.Tensor):
+    """The layer's tiered pool and block map, made for this ssm_state tensor (vLLM's profiling
+    run calls the layer before the real cache exists; a new cache makes a new pool)."""
     st = mixer.nssm
-    if st["pool"] is None:
+    src = (ssm_state.data_ptr(), tuple(ssm_state.shape))
+    if st.get("pool") is None or st.get("src") != src:
         from .pool import TieredSlotPool
-        S, H, P, N = ssm_state.shape
-        st["pool"] = TieredSlotPool(1, S, H, P, N, mixer.n_groups, st["pb"], st["c"], st["cold"],
-                                    torch.bfloat16, ssm_state.device, max_batch=S)
+        nb, H, P, N = ssm_state.shape
+        slots = int(os.environ.get("NESTED_SSM_SLOTS", "0")) or _max_num_seqs() + 64
+        st["pool"] = TieredSlotPool(1, slots, H, P, N, mixer.n_groups, st["pb"], st["c"], st["cold"],
+                                    torch.bfloat16, ssm_state.device, max_batch=max(slots, 8192))
+        st["map"] = torch.full((nb,), -1, dtype=torch.int32, device=ssm_state.device)   # block -> slot
+        st["slotmap"] = SlotMap(slots)
+        st["src"] = src
     return st["pool"]
 
 
-def prefill(mixer, ssm_state: torch.Tensor, slots: torch.Tensor) -> None:
-    """After vLLM wrote the prefill's final states into ``ssm_state[slots]``: split them into
-    the tiered pool (scale/vllm_v4_patch.py:123-137)."""
+def prefill(mixer, ssm_state: torch.Tensor, slots: torch.Tensor, decode_slots: torch.Tensor | None = None) -> None:
+    """After vLLM wrote the prefill's final states into ``ssm_state[slots]`` (block ids): give
+    the blocks tiered-pool slots and split the states into them (scale/vllm_v4_patch.py:123-137).
+    ``decode_slots``: this step's decode blocks (kept when slots are reclaimed)."""
     if mixer.nssm is None:
         return
     from .ops import prefill_split
     if slots.dim() > 1:
         slots = slots.reshape(-1)
     pool = _pool(mixer, ssm_state)
-    prefill_split(pool, 0, ssm_state[slots].float().contiguous(), slots.to(torch.int32))
+    st = mixer.nssm
+    blocks = slots.tolist()
+    live = decode_slots.reshape(-1).tolist() if decode_slots is not None else []
+    comp, freed = st["slotmap"].assign(blocks, live)
+    dev = ssm_state.device
+    if freed:
+        st["map"][torch.tensor(freed, dtype=torch.long, device=dev)] = -1
+    comp_t = torch.tensor(comp, dtype=torch.int32, device=dev)
+    st["map"][slots.long()] = comp_t
+    prefill_split(pool, 0, ssm_state[slots].float().contiguous(), comp_t)
 
 
 def decode(mixer, ssm_state, x, dt_raw, B, C, slots_in, slots_out, out) -> None:
@@ -180,7 +245,8 @@ def decode(mixer, ssm_state, x, dt_raw, B, C, slots_in, slots_out, out) -> None:
     x [b, H*P] or [b, H, P], dt_raw [b, H] before dt_bias and softplus, B / C [b, G*N] as
     split from the conv output (rotated here, on the GPU, by R), slots [b] (or vLLM's [b, 1])
     with NULL_BLOCK_ID on padded rows, out [b, H, P] (vLLM's preallocated output).  The state
-    lives in the tiered pool; ``ssm_state`` only sizes it on first use."""
+    lives in the tiered pool, reached through the block map (an unmapped block, the null block of
+    padded rows among them, is skipped)."""
     from .ops import tiered_state_update
     if slots_in is not slots_out and slots_in.data_ptr() != slots_out.data_ptr():
         raise NotImplementedError("nested_ssm vLLM hook: prefix caching of Mamba states is not supported")
@@ -192,12 +258,14 @@ def decode(mixer, ssm_state, x, dt_raw, B, C, slots_in, slots_out, out) -> None:
         st["A"] = mixer.A.detach().float().reshape(-1).contiguous()
         st["D"] = mixer.D.detach().float().reshape(-1).contiguous()
         st["dt_bias"] = mixer.dt_bias.detach().float().reshape(-1).contiguous()
+    comp = st["map"][slots_in.reshape(-1).long()]   # block -> slot, -1 when unmapped
     bf = torch.bfloat16
     x3 = x.reshape(b, H, P)
     if x3.dtype != bf:
         x3 = x3.to(bf)
     tiered_state_update(pool, 0, x3, dt_raw, st["A"], B.reshape(b, G, -1).to(bf), C.reshape(b, G, -1).to(bf),
-                        st["D"], st["dt_bias"], True, slots_in, NULL_BLOCK_ID, out, mixer.nssm_R, 0.0)
+                        st["D"], st["dt_bias"], True, comp, -1, out, mixer.nssm_R, 0.0,
+                        st.get("readout", "stale"))
 
 
 # --------------------------------------------------------------------------
@@ -226,7 +294,8 @@ PATCHES = [
      "                ssm_state[state_indices_tensor_p] = varlen_states\n",
      "                if self.nssm is not None:  # [nested_ssm] final states -> tiered pool\n"
      "                    from nested_ssm_b200 import vllm_hook as _nssm\n"
-     "                    _nssm.prefill(self, ssm_state, state_indices_tensor_p)\n"),
+     "                    _nssm.prefill(self, ssm_state, state_indices_tensor_p,\n"
+     "                                  state_indices_tensor_d if has_decode else None)\n"),
     (MIXER, "after",
      "            hidden_states_d, B_d, C_d = self.split_hidden_states_B_C_fn(\n"
      "                hidden_states_B_C_d\n"

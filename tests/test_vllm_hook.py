@@ -15,11 +15,12 @@ from nested_ssm_b200 import vllm_hook as VH
 def test_config_from_env_defaults_and_errors():
     assert VH.config_from_env({}) is None
     cfg = VH.config_from_env({"NESTED_SSM_CKPT": "r.pt"})
-    assert cfg == dict(ckpt="r.pt", mode="fresh", pb=32, c=4, cold="bf16")   # scale/vllm_v4_patch.py:28-38
+    assert cfg == dict(ckpt="r.pt", mode="fresh", pb=32, c=4, cold="bf16", readout="stale")   # vllm_v4_patch.py:28-38
     cfg = VH.config_from_env({"NESTED_SSM_CKPT": "r.pt", "NESTED_SSM_MODE": "v4", "NESTED_SSM_PB": "16",
-                              "NESTED_SSM_C": "8", "NESTED_SSM_COLD": "fp8"})
-    assert cfg == dict(ckpt="r.pt", mode="v4", pb=16, c=8, cold="fp8")
-    for bad in ({"NESTED_SSM_MODE": "v5"}, {"NESTED_SSM_COLD": "fp4"}, {"NESTED_SSM_C": "0"}):
+                              "NESTED_SSM_C": "8", "NESTED_SSM_COLD": "fp8", "NESTED_SSM_READOUT": "corr"})
+    assert cfg == dict(ckpt="r.pt", mode="v4", pb=16, c=8, cold="fp8", readout="corr")
+    for bad in ({"NESTED_SSM_MODE": "v5"}, {"NESTED_SSM_COLD": "fp4"}, {"NESTED_SSM_C": "0"},
+                {"NESTED_SSM_READOUT": "exact"}):
         with pytest.raises(ValueError):
             VH.config_from_env({"NESTED_SSM_CKPT": "r.pt", **bad})
 
@@ -74,7 +75,7 @@ def test_apply_ckpt_sets_rotation_decay_and_mode(tmp_path):
         assert torch.equal(m.dt_bias.data, d["decay"]["dt_bias"][i])
         assert m.nssm is None                                     # fresh mode: R only
     VH.apply_ckpt(model, {"NESTED_SSM_CKPT": path, "NESTED_SSM_MODE": "v4", "NESTED_SSM_COLD": "fp8"})
-    assert mixers[1].nssm == dict(pb=32, c=4, cold="fp8", pool=None)
+    assert mixers[1].nssm == dict(pb=32, c=4, cold="fp8", readout="stale", pool=None)
 
 
 def _vllm_copy(tmp_path):
@@ -110,3 +111,18 @@ def test_installer_patches_a_copy_of_vllm_idempotently(tmp_path):
 def test_installer_refuses_a_source_without_the_anchor():
     with pytest.raises(ValueError, match="anchor"):
         VH.patch_source("def f():\n    pass\n", "after", "missing anchor\n", "x = 1\n", "f.py")
+
+
+def test_slot_map_assigns_reuses_and_reclaims():
+    """The hook's block -> pool-slot map on the host: a block keeps its slot, a full map gives
+    back the slots of blocks that neither decode nor prefill this step, and more live sequences
+    than slots is an error."""
+    m = VH.SlotMap(4)
+    s1, freed = m.assign([10, 20, 30], [])
+    assert len(set(s1)) == 3 and freed == []
+    s2, _ = m.assign([20], [10, 30])                      # a block already mapped keeps its slot
+    assert s2 == [s1[1]]
+    s3, freed = m.assign([40, 50], [10])                  # one free slot, two needed: 20, 30 finished
+    assert sorted(freed) == [20, 30] and len(set(s3)) == 2 and s1[0] not in s3
+    with pytest.raises(RuntimeError, match="exceed"):
+        m.assign([60, 70, 80], [10, 40, 50])

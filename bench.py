@@ -87,7 +87,7 @@ def parse():
                     help="only the serving-engine decode (vLLM 0.22, stock against the tiered hook) and print its JSON")
     ap.add_argument("--vllm-arms", default="vllm,ours")
     ap.add_argument("--vllm-mem", type=float, default=0.6, help="vLLM gpu_memory_utilization, stock arm")
-    ap.add_argument("--vllm-mem-ours", type=float, default=0.6,
+    ap.add_argument("--vllm-mem-ours", type=float, default=0.72,
                     help="vLLM gpu_memory_utilization with the hook (its tiered pools, max_num_seqs + 64 slots "
                          "per layer, are allocated after vLLM's cache)")
     ap.add_argument("--vllm-blocks", type=int, default=0, help="vLLM num_gpu_blocks_override (0: vLLM's choice)")
@@ -1213,6 +1213,9 @@ def vllm_e2e(args):
         env = dict(os.environ)
         env["PYTHONPATH"] = REPO + (os.pathsep + env["PYTHONPATH"] if env.get("PYTHONPATH") else "")
         base = arm[:-len("_eager")] if arm.endswith("_eager") else arm   # _eager: no CUDA graphs
+        if base == "ours_fresh":   # the hook in fresh mode, identity R: vLLM's own update, the hook's copies
+            env["PYTHONPATH"] = vllm_shadow(root) + os.pathsep + env["PYTHONPATH"]
+            env.update(NESTED_SSM_CKPT=vllm_rotation_ckpt(root, identity=True), NESTED_SSM_MODE="fresh")
         if base in ("ours", "ours_exact"):
             exact = base == "ours_exact"
             env["PYTHONPATH"] = vllm_shadow(root) + os.pathsep + env["PYTHONPATH"]

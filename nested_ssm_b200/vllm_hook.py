@@ -142,7 +142,8 @@ def apply_ckpt(model, env=None) -> int:
         if cfg["mode"] == "v4":
             if getattr(m, "num_spec", 0):
                 raise NotImplementedError("nested_ssm vLLM hook: speculative decoding is not supported")
-            m.nssm = dict(pb=cfg["pb"], c=cfg["c"], cold=cfg["cold"], readout=cfg["readout"], pool=None)
+            m.nssm = dict(pb=cfg["pb"], c=cfg["c"], cold=cfg["cold"], readout=cfg["readout"], pool=None,
+                          slots=_pool_slots())
     print(f"{MARK} ckpt {cfg['ckpt']} applied to {len(mixers)} mixers (mode={cfg['mode']} "
           f"pb={cfg['pb']} c={cfg['c']} cold={cfg['cold']} readout={cfg['readout']})", flush=True)
     return len(mixers)
@@ -192,12 +193,16 @@ class SlotMap:
         return [self.of_block[k] for k in blocks], freed
 
 
-def _max_num_seqs() -> int:
+def _pool_slots() -> int:
+    """Tiered-pool slots per layer: NESTED_SSM_SLOTS, else the engine's max_num_seqs + 64 (read
+    while the model is built, when vLLM's config is current), else 320."""
+    if int(os.environ.get("NESTED_SSM_SLOTS", "0")) > 0:
+        return int(os.environ["NESTED_SSM_SLOTS"])
     try:
         from vllm.config import get_current_vllm_config
-        return int(get_current_vllm_config().scheduler_config.max_num_seqs)
+        return int(get_current_vllm_config().scheduler_config.max_num_seqs) + 64
     except Exception:   # outside a vLLM engine (tests)
-        return 256
+        return 320
 
 
 def _pool(mixer, ssm_state: torch.Tensor):
@@ -208,7 +213,7 @@ def _pool(mixer, ssm_state: torch.Tensor):
     if st.get("pool") is None or st.get("src") != src:
         from .pool import TieredSlotPool
         nb, H, P, N = ssm_state.shape
-        slots = int(os.environ.get("NESTED_SSM_SLOTS", "0")) or _max_num_seqs() + 64
+        slots = st.get("slots") or _pool_slots()
         st["pool"] = TieredSlotPool(1, slots, H, P, N, mixer.n_groups, st["pb"], st["c"], st["cold"],
                                     torch.bfloat16, ssm_state.device, max_batch=max(slots, 8192))
         st["map"] = torch.full((nb,), -1, dtype=torch.int32, device=ssm_state.device)   # block -> slot

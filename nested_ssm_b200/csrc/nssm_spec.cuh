@@ -377,6 +377,16 @@ __global__ void __launch_bounds__(128 * TPR) commit_step_kernel(const SpecParams
   const int g = h / HG;
   const int64_t sh = (int64_t)slot * p.H + h;
   const int cp = ring_dt_stride(c);
+  // the hot slice is loaded with the bookkeeping, before the accept count is known (a row
+  // that keeps no token only wastes the read)
+  float4* hot4 = reinterpret_cast<float4*>(p.hot + sh * (int64_t)Pn * PB);
+  const int nh = Pn * LPR;
+  float4 hv[HCH];
+#pragma unroll
+  for (int kk = 0; kk < HCH; ++kk) {
+    const int i = kk * T + tid;
+    if (i < nh) hv[kk] = hot4[i];
+  }
   int t0 = 0;
   if (tid == 0) {
     const int k = q.accept[b];
@@ -391,14 +401,6 @@ __global__ void __launch_bounds__(128 * TPR) commit_step_kernel(const SpecParams
     if (lead) q.flush_idx[b] = -1;
     if (k < 0 && tid == 0 && p.status) atomicOr(p.status, STATUS_SPEC_WINDOW);
     return;
-  }
-  float4* hot4 = reinterpret_cast<float4*>(p.hot + sh * (int64_t)Pn * PB);
-  const int nh = Pn * LPR;
-  float4 hv[HCH];
-#pragma unroll
-  for (int kk = 0; kk < HCH; ++kk) {
-    const int i = kk * T + tid;
-    if (i < nh) hv[kk] = hot4[i];
   }
   const float A_h = p.A[h];
   float glog = 0.0f;

@@ -51,3 +51,26 @@ def test_model_e2e_harness_on_cpu():
         assert a["decode_tokens_per_s"] > 0 and a["decode_ms_per_token"] > 0
     # the reference's bf16-cold tiered decode of an fp32 model picks the same greedy tokens here
     assert arms["reference"]["tokens_crc"] == arms["hf"]["tokens_crc"]
+
+
+def test_vllm_leg_model_dir_and_shadow(tmp_path):
+    """The serving-engine leg's pieces on the CPU: the 9B config as vLLM's own NemotronH config
+    class reads it, and the shadow vllm package (file symlinks, the two patched sources) that
+    the hooked arm imports; the installed package is left untouched."""
+    pytest.importorskip("vllm")
+    import importlib.util
+    from nested_ssm_b200 import vllm_hook as VH
+    from vllm.transformers_utils.configs.nemotron_h import NemotronHConfig
+    d = bench.vllm_model_dir(str(tmp_path))
+    cfg = NemotronHConfig.from_pretrained(d)
+    assert cfg.hybrid_override_pattern == bench.NEMOTRON_9B_LAYOUT and cfg.mamba_head_dim == 80
+    top = bench.vllm_shadow(str(tmp_path))
+    src = os.path.dirname(importlib.util.find_spec("vllm").origin)
+    for rel, marks in ((VH.MIXER, 5), (VH.NEMOTRON, 2)):
+        path = os.path.join(top, "vllm", rel)
+        assert not os.path.islink(path)
+        text = open(path).read()
+        assert text.count("[nested_ssm]") >= marks
+        assert "[nested_ssm]" not in open(os.path.join(src, rel)).read()
+    assert os.path.islink(os.path.join(top, "vllm", "__init__.py"))
+    assert "_nssm.apply_ckpt(self)  # [nested_ssm] dummy weights" in open(os.path.join(top, "vllm", VH.NEMOTRON)).read()

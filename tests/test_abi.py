@@ -87,3 +87,41 @@ def test_pool_refuses_cpu_device():
         TieredSlotPool(1, 2, 4, 8, 32, 1, 8, 2, device="cpu")
     with pytest.raises(ValueError):
         TieredSlotPool(1, 2, 4, 8, 32, 1, 40, 2, device="cpu")             # hot >= dstate
+
+
+def _fake_pool_and_args():
+    """A pool and step args whose pointers are never dereferenced (every case below is
+    answered by host-side validation)."""
+    p = _lib.NssmPool()
+    p.num_slots, p.nheads, p.headdim, p.dstate, p.ngroups, p.hot_dim, p.chunk = 8, 128, 80, 128, 8, 32, 4
+    p.cold_dtype, p.io_dtype = _lib.NSSM_F8E4M3, _lib.NSSM_BF16
+    for i, f in enumerate(("hot", "cold", "cold_scale", "glog", "t", "ring_x", "ring_dt", "ring_b")):
+        setattr(p, f, 0x10000 * (i + 1))
+    a = _lib.NssmStepArgs()
+    a.batch, a.io_dtype, a.dt_dtype, a.out_dtype = 4, _lib.NSSM_BF16, _lib.NSSM_BF16, _lib.NSSM_BF16
+    for i, f in enumerate(("x", "dt", "A", "B", "C", "out")):
+        setattr(a, f, 0x100000 * (i + 1))
+    return p, a
+
+
+def test_spec_entry_points_validate_on_the_host():
+    lib = _lib.load()
+    assert lib.nssm_sizeof_token_args() == C.sizeof(_lib.NssmTokenArgs)
+    # rotated B and C of batch * ntok rows, then one int32 per row (256-byte rounded)
+    assert lib.nssm_spec_workspace_bytes(448, 4, 8, 128, _lib.NSSM_BF16, 1) == 2 * 448 * 4 * 8 * 128 * 2 + 1792
+    assert lib.nssm_spec_workspace_bytes(448, 4, 8, 128, _lib.NSSM_BF16, 0) == 1792
+    p, a = _fake_pool_and_args()
+    t = _lib.NssmTokenArgs()
+    t.ntok = 2
+    assert lib.nssm_verify_step(C.byref(p), C.byref(a), None, None) == _lib.NSSM_ERR_INVALID
+    assert lib.nssm_commit_step(C.byref(p), C.byref(a), C.byref(t), None) == _lib.NSSM_ERR_INVALID   # accept NULL
+    assert "accept" in lib.nssm_last_error().decode()
+    a.mode = _lib.NSSM_MODE_CORR
+    assert lib.nssm_verify_step(C.byref(p), C.byref(a), C.byref(t), None) == _lib.NSSM_ERR_UNSUPPORTED
+    a.mode = _lib.NSSM_MODE_STALE
+    t.ntok = 5                                                      # longer than the chunk (4)
+    assert lib.nssm_verify_step(C.byref(p), C.byref(a), C.byref(t), None) == _lib.NSSM_ERR_INVALID
+    assert "chunk" in lib.nssm_last_error().decode()
+    t.ntok = 0
+    assert lib.nssm_verify_step(C.byref(p), C.byref(a), C.byref(t), None) == _lib.NSSM_ERR_INVALID
+    assert lib.nssm_draft_step(C.byref(p), None, 1, C.byref(a), None) == _lib.NSSM_ERR_INVALID   # draft NULL

@@ -128,3 +128,28 @@ def test_slot_map_assigns_reuses_and_reclaims():
     assert sorted(freed) == [20, 30] and len(set(s3)) == 2 and s1[0] not in s3
     with pytest.raises(RuntimeError, match="exceed"):
         m.assign([60, 70, 80], [10, 40, 50])
+
+
+def test_slot_map_under_a_simulated_block_allocator():
+    """Requests arrive and finish at random; each takes a free block id from a pool of 8x the
+    slots (as vLLM 0.22's shared block pool does), prefills once and then decodes every step.
+    Live sequences always hold distinct slots, a sequence's slot never changes while it lives,
+    and the map never needs more slots than live sequences + the step's prefills."""
+    import random
+    rng = random.Random(3)
+    cap, nblocks = 16, 128
+    m = VH.SlotMap(cap)
+    free_blocks = list(range(1, nblocks))          # block 0: vLLM's null block
+    live = {}                                       # block -> slot given at its prefill
+    for step in range(400):
+        for k in [k for k in live if rng.random() < 0.1]:   # finished requests free their block
+            del live[k]
+            free_blocks.append(k)
+        rng.shuffle(free_blocks)
+        new = [free_blocks.pop() for _ in range(min(rng.randint(0, 4), cap - len(live)))]
+        slots, _ = m.assign(new, list(live))
+        for k, s in zip(new, slots):
+            live[k] = s
+        assert len(set(live.values())) == len(live) <= cap
+        for k, s in live.items():
+            assert m.of_block[k] == s

@@ -71,3 +71,47 @@ def test_windows_across_a_chunk_boundary_are_refused():
         O.verify_steps(pool, slots, xs, dts, Bs, Cs, prm["A"], prm["D"], prm["dt_bias"])
     with pytest.raises(ValueError):
         O.commit_steps(pool, slots, torch.tensor([4, 3]), xs, dts, Bs, prm["A"], prm["dt_bias"])
+
+
+def test_draft_equals_coldoff_readout_on_random_cases():
+    """The hot-only draft's y and hot evolution are the tiered step's in mode coldoff (the
+    readout ignores the cold slice; the hot update never reads it), for every hot width."""
+    for pb in (16, 32, 64):
+        case = Hh.make_case(b=3, S=5, H=16, G=2, pb=pb, c=4, cold="fp8", steps=6, seed=pb)
+        prm = case["prm"]
+        slots = torch.tensor([4, 0, 2])
+        pool = Hh.oracle_pool(case)
+        O.prefill_split(pool, slots, case["state0"])
+        draft = pool.hot.clone()
+        for s in range(6):
+            Br, Cr = Hh.rotated(case, s)
+            yd = O.draft_step(draft, slots, case["xs"][s], case["dts"][s], Br, Cr, prm["A"], prm["D"], prm["dt_bias"])
+            yc = O.tiered_step(pool, slots, case["xs"][s], case["dts"][s], Br, Cr, prm["A"], prm["D"], prm["dt_bias"],
+                               mode="coldoff")
+            torch.testing.assert_close(yd, yc, rtol=1e-6, atol=1e-7)
+            assert torch.equal(draft[slots], pool.hot[slots])
+
+
+def test_verify_commit_cover_a_long_chunk():
+    """c = 16 from phase 5: verify of the remaining 11 tokens, then a commit that stops short
+    of the boundary for some rows and completes the chunk (a flush) for others."""
+    case = Hh.make_case(b=3, S=4, H=16, G=2, pb=32, c=16, cold="fp8", steps=16, seed=9)
+    prm = case["prm"]
+    slots = torch.tensor([3, 1, 0])
+    pools = [Hh.oracle_pool(case) for _ in range(2)]
+    for p_ in pools:
+        O.prefill_split(p_, slots, case["state0"])
+        for s in range(5):
+            Br, Cr = Hh.rotated(case, s)
+            O.tiered_step(p_, slots, case["xs"][s], case["dts"][s], Br, Cr, prm["A"], prm["D"], prm["dt_bias"])
+    xs, dts, Bs, Cs = _stacked(case, 5, 11)
+    O.verify_steps(pools[0], slots, xs, dts, Bs, Cs, prm["A"], prm["D"], prm["dt_bias"])
+    accept = torch.tensor([11, 4, 0])
+    O.commit_steps(pools[0], slots, accept, xs, dts, Bs, prm["A"], prm["dt_bias"])
+    for j in range(11):
+        sl = slots.clone()
+        sl[accept <= j] = -1
+        O.tiered_step(pools[1], sl, xs[:, j], dts[:, j], Bs[:, j], Cs[:, j], prm["A"], prm["D"], prm["dt_bias"])
+    for name in ("hot", "cold", "scale", "glog", "t", "ring_x", "ring_dt", "ring_b"):
+        assert torch.equal(getattr(pools[0], name), getattr(pools[1], name)), name
+    assert pools[0].t[[3, 1, 0]].tolist() == [16, 9, 5] and float(pools[0].glog[3].abs().sum()) == 0.0

@@ -225,7 +225,9 @@ def _pool(mixer, ssm_state: torch.Tensor):
 def prefill(mixer, ssm_state: torch.Tensor, slots: torch.Tensor, decode_slots: torch.Tensor | None = None) -> None:
     """After vLLM wrote the prefill's final states into ``ssm_state[slots]`` (block ids): give
     the blocks tiered-pool slots and split the states into them (scale/vllm_v4_patch.py:123-137).
-    ``decode_slots``: this step's decode blocks (kept when slots are reclaimed)."""
+    ``decode_slots``: this step's decode blocks (kept when slots are reclaimed).  The block ids
+    are read on the host: one synchronisation per prefill step (vLLM never captures batches with
+    prefills in CUDA graphs; decode steps, which may be captured, do not synchronise)."""
     if mixer.nssm is None:
         return
     from .ops import prefill_split
